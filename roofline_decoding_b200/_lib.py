@@ -1,0 +1,111 @@
+"""ctypes binding of libw4b200.so, the C ABI declared in include/w4b200.h.
+
+Loading fails loudly: there is no fallback implementation behind this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libw4b200.so")
+HEADER_PATH = Path(__file__).resolve().parent.parent / "include" / "w4b200.h"
+
+W4_OK, W4_ERR_INVALID_ARG, W4_ERR_ALIGNMENT, W4_ERR_UNSUPPORTED, W4_ERR_CUDA, W4_ERR_DEVICE = range(6)
+W4_F16, W4_BF16 = 0, 1
+# w4_pack input dtypes (the reference packer accepts any float tensor and
+# works on its fp32 value).
+W4_PACK_F16, W4_PACK_BF16, W4_PACK_F32 = 0, 1, 2
+
+
+class W4Error(RuntimeError):
+    """A CUDA-side failure reported by the library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class GemvConfig(ctypes.Structure):
+    _fields_ = [
+        ("strips", ctypes.c_int),
+        ("row_groups", ctypes.c_int),
+        ("stages", ctypes.c_int),
+        ("split", ctypes.c_int),
+        ("pdl", ctypes.c_int),
+    ]
+
+    def as_tuple(self) -> tuple[int, int, int, int, int]:
+        return (self.strips, self.row_groups, self.stages, self.split, self.pdl)
+
+    @classmethod
+    def from_tuple(cls, t) -> "GemvConfig":
+        return cls(*[int(v) for v in t])
+
+    def __repr__(self) -> str:
+        return ("GemvConfig(strips=%d, row_groups=%d, stages=%d, split=%d, pdl=%d)"
+                % self.as_tuple())
+
+
+_c_int, _c_void_p, _c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/w4b200.h
+SIGNATURES = {
+    "w4_version": (_c_int, []),
+    "w4_status_string": (ctypes.c_char_p, [_c_int]),
+    "w4_last_error": (ctypes.c_char_p, []),
+    "w4_init": (_c_int, [_c_int]),
+    "w4_pack": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_int,
+                         _c_void_p]),
+    "w4_dequant": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p]),
+    "w4_gemv": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int,
+                         _c_int, _c_int, _c_int, _c_int, _c_void_p]),
+    "w4_gemv_ex": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int,
+                            _c_int, _c_int, ctypes.POINTER(GemvConfig), _c_void_p]),
+    "w4_gemv_default_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int,
+                                        ctypes.POINTER(GemvConfig)]),
+    "w4_device_error": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Returns the loaded library; raises if the shared object is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise ImportError(
+                    f"{LIB_PATH.name} is not built; run `python -c 'import __graft_entry__ as g; "
+                    f"g.build()'` (or roofline_decoding_b200/_build.py) first")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    """Raises the Python exception matching a w4_status."""
+    if status == W4_OK:
+        return
+    lib = load()
+    msg = f"{what}: {lib.w4_status_string(status).decode()}: {lib.w4_last_error().decode()}"
+    if status in (W4_ERR_INVALID_ARG, W4_ERR_ALIGNMENT):
+        raise ValueError(msg)
+    if status == W4_ERR_UNSUPPORTED:
+        raise NotImplementedError(msg)
+    raise W4Error(status, msg)
+
+
+def device_error(device: int) -> int:
+    """Reads and clears the kernels' device-side error word (synchronises)."""
+    code = ctypes.c_int(0)
+    check(load().w4_device_error(device, ctypes.byref(code)), "w4_device_error")
+    return code.value

@@ -1,0 +1,240 @@
+// w4_api.cu - extern "C" entry points of libw4b200.so (declared in
+// include/w4b200.h): argument validation, one-off device set-up and dispatch.
+#include "w4_internal.h"
+
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+namespace w4 {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_init_mutex;
+constexpr int kMaxDevices = 64;
+DeviceInfo g_devices[kMaxDevices];
+bool g_ready[kMaxDevices] = {};
+EncodeTiledFn g_encode = nullptr;
+
+__device__ int g_error_word = 0;
+}  // namespace
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(W4_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+const DeviceInfo& device_info(int device) { return g_devices[device]; }
+EncodeTiledFn encode_tiled_fn() { return g_encode; }
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(W4_ERR_UNSUPPORTED, "device %d", *dev);
+  if (!g_ready[*dev]) return w4_init(*dev);
+  return W4_OK;
+}
+
+namespace {
+
+int init_locked(int device) {
+  if (g_ready[device]) return W4_OK;
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess)
+    return cuda_fail(e, "cudaSetDevice");
+  DeviceInfo di;
+  int st = W4_OK;
+  do {
+    if ((e = cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, device)) ||
+        (e = cudaDeviceGetAttribute(&di.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                                    device)) ||
+        (e = cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, device)) ||
+        (e = cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, device))) {
+      st = cuda_fail(e, "cudaDeviceGetAttribute");
+      break;
+    }
+    if (di.cc_major != 10 || di.cc_minor != 0) {
+      st = fail(W4_ERR_UNSUPPORTED,
+                "device %d is sm_%d%d; this library is built for sm_100a (B200) only", device,
+                di.cc_major, di.cc_minor);
+      break;
+    }
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        st = fail(W4_ERR_CUDA, "cannot resolve cuTensorMapEncodeTiled from the driver");
+        break;
+      }
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    void* addr = nullptr;
+    if ((e = cudaGetSymbolAddress(&addr, g_error_word)) != cudaSuccess) {
+      st = cuda_fail(e, "cudaGetSymbolAddress(error word)");
+      break;
+    }
+    di.err_word = static_cast<int*>(addr);
+    st = gemv_init_device(di);
+  } while (false);
+  if (prev != device) cudaSetDevice(prev);
+  if (st == W4_OK) {
+    g_devices[device] = di;
+    g_ready[device] = true;
+  }
+  return st;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_dtype(int dt, const char* what) {
+  if (dt != W4_F16 && dt != W4_BF16)
+    return fail(W4_ERR_INVALID_ARG, "%s dtype %d is neither W4_F16 nor W4_BF16", what, dt);
+  return W4_OK;
+}
+
+}  // namespace
+}  // namespace w4
+
+using namespace w4;
+
+extern "C" {
+
+int w4_version(void) { return W4B200_VERSION; }
+
+const char* w4_status_string(int status) {
+  switch (status) {
+    case W4_OK: return "W4_OK";
+    case W4_ERR_INVALID_ARG: return "W4_ERR_INVALID_ARG";
+    case W4_ERR_ALIGNMENT: return "W4_ERR_ALIGNMENT";
+    case W4_ERR_UNSUPPORTED: return "W4_ERR_UNSUPPORTED";
+    case W4_ERR_CUDA: return "W4_ERR_CUDA";
+    case W4_ERR_DEVICE: return "W4_ERR_DEVICE";
+    default: return "W4_ERR_UNKNOWN";
+  }
+}
+
+const char* w4_last_error(void) { return g_last_error.c_str(); }
+
+int w4_init(int device) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(W4_ERR_INVALID_ARG, "device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_init_mutex);
+  return init_locked(device);
+}
+
+int w4_pack(const void* w, int w_dtype, int32_t* packed, void* scales, int K, int N,
+            int group_size, void* stream) {
+  if (!w || !packed || !scales) return fail(W4_ERR_INVALID_ARG, "w4_pack: null pointer");
+  if (w_dtype != W4_PACK_F16 && w_dtype != W4_PACK_BF16 && w_dtype != W4_PACK_F32)
+    return fail(W4_ERR_INVALID_ARG, "w4_pack: w dtype %d unknown", w_dtype);
+  if (K <= 0 || N <= 0) return fail(W4_ERR_INVALID_ARG, "w4_pack: K=%d N=%d", K, N);
+  if (group_size <= 0 || group_size % 8 != 0 || K % group_size != 0)
+    return fail(W4_ERR_INVALID_ARG,
+                "w4_pack: group_size=%d must be a positive multiple of 8 dividing K=%d",
+                group_size, K);
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  cudaError_t e = launch_pack(w, w_dtype, packed, scales, K, N, group_size, (cudaStream_t)stream);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_pack launch");
+}
+
+int w4_dequant(const int32_t* packed, const void* scales, void* out, int out_dtype, int K, int N,
+               void* stream) {
+  if (!packed || !scales || !out) return fail(W4_ERR_INVALID_ARG, "w4_dequant: null pointer");
+  int st = check_dtype(out_dtype, "w4_dequant out");
+  if (st != W4_OK) return st;
+  if (K <= 0 || N <= 0 || K % 128 != 0 || N % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_dequant: K=%d must be a multiple of 128, N=%d of 8", K,
+                N);
+  if (!aligned16(packed) || !aligned16(scales) || !aligned16(out))
+    return fail(W4_ERR_ALIGNMENT, "w4_dequant: pointers must be 16-byte aligned");
+  int dev;
+  if ((st = current_device(&dev)) != W4_OK) return st;
+  cudaError_t e = launch_dequant(packed, scales, out, out_dtype == W4_BF16, K, N,
+                                 (cudaStream_t)stream);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_dequant launch");
+}
+
+static int gemv_check(const void* x, int x_dtype, const int32_t* packed, const void* scales,
+                      void* y, int y_dtype, int M, int K, int N) {
+  if (!x || !packed || !scales || !y) return fail(W4_ERR_INVALID_ARG, "w4_gemv: null pointer");
+  int st = check_dtype(x_dtype, "w4_gemv x");
+  if (st != W4_OK) return st;
+  if ((st = check_dtype(y_dtype, "w4_gemv y")) != W4_OK) return st;
+  if (M < 1 || M > W4B200_MAX_M)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv: M=%d outside 1..%d", M, W4B200_MAX_M);
+  if (K <= 0 || K % 128 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv: K=%d must be a positive multiple of 128", K);
+  if (N <= 0 || N % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv: N=%d must be a positive multiple of 8", N);
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(scales) || !aligned16(y))
+    return fail(W4_ERR_ALIGNMENT, "w4_gemv: pointers must be 16-byte aligned");
+  return W4_OK;
+}
+
+int w4_gemv_default_config(int M, int K, int N, int split_k, int num_warps,
+                           w4_gemv_config* out) {
+  if (!out) return fail(W4_ERR_INVALID_ARG, "w4_gemv_default_config: null out");
+  if (M < 1 || M > W4B200_MAX_M || K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_default_config: M=%d K=%d N=%d", M, K, N);
+  if (split_k > 16 || split_k > K / 128)
+    return fail(W4_ERR_INVALID_ARG, "split_k=%d must be <= min(16, K/128=%d)", split_k, K / 128);
+  if (num_warps > 0 && num_warps != 4 && num_warps != 8)
+    return fail(W4_ERR_INVALID_ARG, "num_warps=%d must be 4 or 8", num_warps);
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  return gemv_choose_config(M, K, N, split_k, num_warps, device_info(dev), out);
+}
+
+int w4_gemv(const void* x, int x_dtype, const int32_t* packed, const void* scales, void* y,
+            int y_dtype, int M, int K, int N, int split_k, int num_warps, void* stream) {
+  int st = gemv_check(x, x_dtype, packed, scales, y, y_dtype, M, K, N);
+  if (st != W4_OK) return st;
+  w4_gemv_config c;
+  if ((st = w4_gemv_default_config(M, K, N, split_k, num_warps, &c)) != W4_OK) return st;
+  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, c};
+  return launch_gemv(L, (cudaStream_t)stream);
+}
+
+int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed, const void* scales, void* y,
+               int y_dtype, int M, int K, int N, const w4_gemv_config* cfg, void* stream) {
+  int st = gemv_check(x, x_dtype, packed, scales, y, y_dtype, M, K, N);
+  if (st != W4_OK) return st;
+  if (!cfg) return fail(W4_ERR_INVALID_ARG, "w4_gemv_ex: null config");
+  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg};
+  return launch_gemv(L, (cudaStream_t)stream);
+}
+
+int w4_device_error(int device, int* code) {
+  if (!code) return fail(W4_ERR_INVALID_ARG, "w4_device_error: null out");
+  int st = w4_init(device);
+  if (st != W4_OK) return st;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != device) cudaSetDevice(device);
+  int zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(code, g_error_word, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(int));
+  if (prev != device) cudaSetDevice(prev);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_device_error");
+}
+
+}  // extern "C"

@@ -1,0 +1,505 @@
+// w4_gemv.cu - fused W4A16 dequantise + GEMV / small-M GEMM for sm_100a.
+//
+// Computes y[m, n] = sum_k x[m, k] * (q[k, n] - 8) * s[k / 128, n] for
+// 1 <= M <= 16, the operation of roofline/kernels.py:93-128 (_fused_gemv_kernel)
+// and :163-208 (_fused_gemv_v3_kernel), on the reference's packed layout.
+//
+// Work decomposition
+//   CTA tile    : 32*SW output columns x one K slice (a "split").
+//   Warps       : SW*RG compute warps + 1 producer warp. Compute warp w owns
+//                 strip w % SW (32 columns) and row group w / SW.
+//   Stage       : RG K-groups (RG * 16 packed rows) for all SW strips, i.e.
+//                 SW TMA boxes of [RG*16 rows x 32 int32] (128B-swizzled) plus
+//                 one box of RG x 32*SW fp16 scales. The producer streams
+//                 stages through an mbarrier ring of `stages` slots.
+//   Split-K     : the splits of one column tile form a thread-block cluster;
+//                 after the K loop every CTA leaves its fp32 partial in shared
+//                 memory and the cluster sums them over DSMEM in rank order.
+//                 No atomics, no workspace: results are bit-reproducible.
+//
+// Inner product on the tensor cores (swap-AB): A = W^T tile (16 columns x 16
+// k), B = x^T (16 k x 8 batch rows), D fp32. A thread's 16-byte shared load
+// yields 4 columns x 8 k of one packed row; LOP3 turns each word into four
+// f16x2/bf16x2 pairs of exact (q - 8) values. The k order inside an MMA is a
+// permutation of the true k order (nibbles (0,4),(1,5) | (2,6),(3,7) of the
+// rows 2t, 2t+1 of each 8-row octet); x is staged in shared memory in the same
+// permuted order, so the sum is unchanged. The per-group scale multiplies the
+// fp32 group sum once per (group, column) - fused in registers.
+#include "w4_internal.h"
+#include "w4_ptx.cuh"
+
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+namespace cg = cooperative_groups;
+
+namespace w4 {
+
+struct GemvParams {
+  const void* x;  // [M, K] fp16 / bf16
+  void* y;        // [M, N] fp16 / bf16
+  int M, K, N;
+  int groups_total;      // K / 128
+  int groups_per_split;  // K groups handled by one CTA
+  int stages;            // ring depth
+  int y_bf16;
+  int* err;  // device error word
+};
+
+template <int SW, int RG>
+struct TileShape {
+  static constexpr int kCW = SW * RG;              // compute warps
+  static constexpr int kThreads = (kCW + 1) * 32;  // + producer warp
+  static constexpr int kNT = 32 * SW;              // output columns per CTA
+  static constexpr int kStripBytes = RG * 16 * 128;
+  static constexpr int kStageBytes = SW * kStripBytes;
+  static constexpr int kScaleBytes = RG * kNT * 2;                // one scale box
+  static constexpr int kScaleSlot = (kScaleBytes + 127) / 128 * 128;  // TMA dst: 128 B aligned
+};
+
+__device__ __forceinline__ void consumer_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void report_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// Reorders the 8 activations of one packed row into the order the MMA
+// fragments consume them: (x0,x4) (x1,x5) (x2,x6) (x3,x7).
+__device__ __forceinline__ uint4 permute_row(uint4 v) {
+  uint4 o;
+  o.x = __byte_perm(v.x, v.z, 0x5410);
+  o.y = __byte_perm(v.x, v.z, 0x7632);
+  o.z = __byte_perm(v.y, v.w, 0x5410);
+  o.w = __byte_perm(v.y, v.w, 0x7632);
+  return o;
+}
+
+template <bool kBF16, int MB, int SW, int RG>
+__global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
+    w4_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_s, const GemvParams p) {
+  using T = TileShape<SW, RG>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int S = p.stages;
+  const int M = p.M;
+  const int rows_slice = p.groups_per_split * 16;
+  const int plane = rows_slice * 16 + 16;  // +16 B: odd batch rows land on other banks
+  uint8_t* s_w = smem;
+  uint8_t* s_sc = s_w + S * T::kStageBytes;
+  uint8_t* s_x = s_sc + S * T::kScaleSlot;
+  float* s_red = reinterpret_cast<float*>(s_x + M * plane);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_red + RG * M * T::kNT);
+  uint64_t* empty = full + S;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * T::kNT;
+  const int g0 = blockIdx.y * p.groups_per_split;
+  const int g1 = min(p.groups_total, g0 + p.groups_per_split);
+  const int n_groups = max(0, g1 - g0);
+  const int n_stages = (n_groups + RG - 1) / RG;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], T::kCW);
+    }
+    fence_mbar_init();
+  }
+  if (warp == T::kCW && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_s);
+  }
+  __syncthreads();
+  // Dependent grids may start their prologue (and their weight stream) now;
+  // they read our output only after their own grid-dependency wait.
+  grid_launch_dependents();
+
+  // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
+  // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
+  float acc[2][MB][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b = 0; b < MB; ++b)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
+
+  if (warp == T::kCW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < n_stages; ++j) {
+        const int slot = j % S;
+        if (j >= S && !mbar_wait(&empty[slot], ((j / S) - 1) & 1)) {
+          report_error(p.err, kErrEmptyWait);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[slot], T::kStageBytes + T::kScaleBytes);
+        const int grp = g0 + j * RG;
+#pragma unroll
+        for (int s = 0; s < SW; ++s)
+          tma_load_2d(s_w + slot * T::kStageBytes + s * T::kStripBytes, &tm_w, &full[slot],
+                      n0 + 32 * s, grp * 16);
+        tma_load_2d(s_sc + slot * T::kScaleSlot, &tm_s, &full[slot], n0, grp);
+        ++issued;
+      }
+      // Do not leave while copies into this CTA's shared memory are in flight.
+      for (int j = max(0, issued - S); j < issued; ++j)
+        if (!mbar_wait(&full[j % S], (j / S) & 1)) report_error(p.err, kErrDrainWait);
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int nct = T::kCW * 32;
+    // x is produced by the previous kernel on the stream: wait for it.
+    grid_dependency_wait();
+    const uint16_t* xg = static_cast<const uint16_t*>(p.x);
+    for (int idx = threadIdx.x; idx < M * rows_slice; idx += nct) {
+      const int m = idx / rows_slice;
+      const int r = idx - m * rows_slice;
+      const int krow = g0 * 16 + r;  // packed row = 8 activations
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (krow < g1 * 16)
+        v = *reinterpret_cast<const uint4*>(xg + (size_t)m * p.K + (size_t)krow * 8);
+      *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = permute_row(v);
+    }
+    consumer_bar_sync(nct);
+
+    const int strip = warp % SW;
+    const int rg = warp / SW;
+    const int g = lane >> 2;
+    const int t = lane & 3;
+    const uint32_t s_w_u32 = smem_u32(s_w);
+    const uint32_t s_sc_u32 = smem_u32(s_sc);
+    const uint32_t s_x_u32 = smem_u32(s_x);
+    bool ok = true;
+
+    for (int j = 0; j < n_stages && ok; ++j) {
+      const int slot = j % S;
+      if (!mbar_wait(&full[slot], (j / S) & 1)) {
+        report_error(p.err, kErrFullWait);
+        ok = false;
+        break;
+      }
+      const int grp = g0 + j * RG + rg;
+      if (grp < g1) {
+        float c[2][MB][4];
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+          for (int b = 0; b < MB; ++b)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[a][b][i] = 0.f;
+
+        const uint32_t box = s_w_u32 + slot * T::kStageBytes + strip * T::kStripBytes;
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int r = rg * 16 + 8 * o + 2 * t + e;  // row inside the strip box
+            // 128B swizzle: 16-byte chunk index XOR (row & 7).
+            const uint4 wv = lds128(box + r * 128 + ((g ^ (r & 7)) << 4));
+            const int xr = (grp - g0) * 16 + 8 * o + 2 * t + e;  // row inside the slice
+            uint4 xb[MB];
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb) {
+              const int m = 8 * mb + g;
+              xb[mb] = (m < M) ? lds128(s_x_u32 + m * plane + xr * 16)
+                               : make_uint4(0u, 0u, 0u, 0u);
+            }
+            uint32_t ha[4], hb[4];
+            unpack_nibbles<kBF16>(wv.x, ha);  // column 4g
+            unpack_nibbles<kBF16>(wv.y, hb);  // column 4g+1
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb) {
+              mma_16816<kBF16>(c[0][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+              mma_16816<kBF16>(c[0][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+            }
+            unpack_nibbles<kBF16>(wv.z, ha);  // column 4g+2
+            unpack_nibbles<kBF16>(wv.w, hb);  // column 4g+3
+#pragma unroll
+            for (int mb = 0; mb < MB; ++mb) {
+              mma_16816<kBF16>(c[1][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+              mma_16816<kBF16>(c[1][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+            }
+          }
+        }
+        // Scales of this group for columns (4g, 4g+1) and (4g+2, 4g+3).
+        const uint32_t sc_row = s_sc_u32 + slot * T::kScaleSlot + (rg * T::kNT + 32 * strip) * 2;
+        const uint32_t s01 = lds32(sc_row + (4 * g) * 2);
+        const uint32_t s23 = lds32(sc_row + (4 * g + 2) * 2);
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&s01));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
+#pragma unroll
+        for (int mb = 0; mb < MB; ++mb) {
+          acc[0][mb][0] = fmaf(f01.x, c[0][mb][0], acc[0][mb][0]);
+          acc[0][mb][1] = fmaf(f01.x, c[0][mb][1], acc[0][mb][1]);
+          acc[0][mb][2] = fmaf(f01.y, c[0][mb][2], acc[0][mb][2]);
+          acc[0][mb][3] = fmaf(f01.y, c[0][mb][3], acc[0][mb][3]);
+          acc[1][mb][0] = fmaf(f23.x, c[1][mb][0], acc[1][mb][0]);
+          acc[1][mb][1] = fmaf(f23.x, c[1][mb][1], acc[1][mb][1]);
+          acc[1][mb][2] = fmaf(f23.y, c[1][mb][2], acc[1][mb][2]);
+          acc[1][mb][3] = fmaf(f23.y, c[1][mb][3], acc[1][mb][3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+
+    // Per-warp partials into s_red[rg][m][col].
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int m = 8 * mb + 2 * t + (i & 1);
+          if (m < M) {
+            const int col = 32 * strip + 4 * g + 2 * a + (i >> 1);
+            s_red[(rg * M + m) * T::kNT + col] = acc[a][mb][i];
+          }
+        }
+  }
+  __syncthreads();
+
+  // Row groups -> plane 0, in a fixed order.
+  const int tile_elems = M * T::kNT;
+  if (RG > 1) {
+    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {
+      float v = s_red[idx];
+#pragma unroll
+      for (int r = 1; r < RG; ++r) v += s_red[r * tile_elems + idx];
+      s_red[idx] = v;
+    }
+  }
+
+  const int nsplit = gridDim.y;
+  auto store = [&](int idx, float v) {
+    const int m = idx / T::kNT;
+    const int n = n0 + (idx - m * T::kNT);
+    if (n < p.N) {
+      if (p.y_bf16)
+        static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v);
+      else
+        static_cast<__half*>(p.y)[(size_t)m * p.N + n] = __float2half_rn(v);
+    }
+  };
+
+  if (nsplit == 1) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) store(idx, s_red[idx]);
+  } else {
+    // Split-K over the cluster: every CTA sums a share of the tile over all
+    // ranks' partials in rank order (DSMEM reads), then writes it.
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int rank = (int)cluster.block_rank();
+    for (int idx = rank * T::kThreads + threadIdx.x; idx < tile_elems;
+         idx += T::kThreads * nsplit) {
+      float v = 0.f;
+      for (int r = 0; r < nsplit; ++r) v += cluster.map_shared_rank(s_red, r)[idx];
+      store(idx, v);
+    }
+    cluster.sync();  // keep this CTA's shared memory alive for the readers
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+namespace {
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemvParams);
+
+template <bool B, int MB, int SW, int RG>
+void* kptr() {
+  return reinterpret_cast<void*>(&w4_gemv_kernel<B, MB, SW, RG>);
+}
+
+template <bool B, int MB>
+void* pick_tile(int sw, int rg) {
+  switch (sw * 16 + rg) {
+    case 1 * 16 + 1: return kptr<B, MB, 1, 1>();
+    case 1 * 16 + 2: return kptr<B, MB, 1, 2>();
+    case 1 * 16 + 4: return kptr<B, MB, 1, 4>();
+    case 1 * 16 + 8: return kptr<B, MB, 1, 8>();
+    case 2 * 16 + 1: return kptr<B, MB, 2, 1>();
+    case 2 * 16 + 2: return kptr<B, MB, 2, 2>();
+    case 2 * 16 + 4: return kptr<B, MB, 2, 4>();
+    case 4 * 16 + 1: return kptr<B, MB, 4, 1>();
+    case 4 * 16 + 2: return kptr<B, MB, 4, 2>();
+    default: return nullptr;
+  }
+}
+
+void* pick_kernel(int bf16, int mb, int sw, int rg) {
+  if (bf16) return mb == 1 ? pick_tile<true, 1>(sw, rg) : pick_tile<true, 2>(sw, rg);
+  return mb == 1 ? pick_tile<false, 1>(sw, rg) : pick_tile<false, 2>(sw, rg);
+}
+
+constexpr int kSW[] = {1, 2, 4};
+
+}  // namespace
+
+size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& c) {
+  const int groups = K / 128;
+  const int gps = (groups + c.split - 1) / c.split;
+  const size_t nt = 32 * (size_t)c.strips;
+  const size_t stage = (size_t)c.strips * c.row_groups * 16 * 128;
+  const size_t scale = ((size_t)c.row_groups * nt * 2 + 127) / 128 * 128;
+  const size_t plane = (size_t)gps * 16 * 16 + 16;
+  return 1024 + c.stages * (stage + scale) + M * plane + c.row_groups * M * nt * 4 +
+         2 * c.stages * sizeof(uint64_t);
+}
+
+int gemv_validate_config(int M, int K, int N, const w4_gemv_config& c, const DeviceInfo& di) {
+  (void)N;
+  if (!pick_kernel(0, 1, c.strips, c.row_groups))
+    return fail(W4_ERR_INVALID_ARG, "unsupported tile strips=%d row_groups=%d", c.strips,
+                c.row_groups);
+  if (c.stages < 2 || c.stages > 8)
+    return fail(W4_ERR_INVALID_ARG, "stages=%d outside 2..8", c.stages);
+  if (c.split < 1 || c.split > 16)
+    return fail(W4_ERR_INVALID_ARG, "split=%d outside 1..16", c.split);
+  if (c.split > K / 128)
+    return fail(W4_ERR_INVALID_ARG, "split=%d exceeds the %d K groups", c.split, K / 128);
+  const size_t smem = gemv_smem_bytes(M, K, c);
+  if (smem > (size_t)di.max_smem_optin)
+    return fail(W4_ERR_UNSUPPORTED,
+                "tile needs %zu B of shared memory (device allows %d); raise split", smem,
+                di.max_smem_optin);
+  return W4_OK;
+}
+
+int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const DeviceInfo& di,
+                       w4_gemv_config* out) {
+  const int groups = K / 128;
+  const int sms = di.sm_count > 0 ? di.sm_count : 148;
+  const int cw = (num_warps == 4) ? 4 : 8;
+  // Widest tile whose column count does not exceed N (fewer, longer rows of
+  // contiguous 128-byte segments per CTA stream better).
+  int sw = 4;
+  while (sw > 1 && 32 * sw > N) sw /= 2;
+  if (cw / sw > 8) sw = cw / 8;
+  const int rg = std::max(1, cw / sw);
+  const int tiles = (N + 32 * sw - 1) / (32 * sw);
+  int split = split_k;
+  if (split <= 0) {
+    // Aim for about two CTAs per SM, keep at least RG groups per split.
+    const int want = (2 * sms + tiles - 1) / tiles;
+    split = std::min({want, 8, std::max(1, groups / rg)});
+    split = std::max(split, 1);
+  }
+  w4_gemv_config c{sw, rg, 4, split, 0};
+  const int gps = (groups + split - 1) / split;
+  const int stages_needed = (gps + rg - 1) / rg;
+  c.stages = std::max(2, std::min(4, stages_needed));
+  // Grow the split until the activation slice fits in shared memory.
+  while (gemv_smem_bytes(M, K, c) > (size_t)di.max_smem_optin && c.split < 16 &&
+         c.split < groups && split_k <= 0)
+    ++c.split;
+  *out = c;
+  return gemv_validate_config(M, K, N, c, di);
+}
+
+static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
+                     uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                     CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int gemv_init_device(const DeviceInfo& di) {
+  for (int b = 0; b < 2; ++b)
+    for (int mb = 1; mb <= 2; ++mb)
+      for (int sw : kSW)
+        for (int rg = 1; rg <= 8; rg *= 2) {
+          void* k = pick_kernel(b, mb, sw, rg);
+          if (!k) continue;
+          cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               di.max_smem_optin);
+          if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max smem)");
+          e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+          if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(cluster)");
+        }
+  return W4_OK;
+}
+
+int launch_gemv(const GemvLaunch& L, cudaStream_t stream) {
+  int dev = 0;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  const DeviceInfo& di = device_info(dev);
+  const w4_gemv_config& c = L.cfg;
+  st = gemv_validate_config(L.M, L.K, L.N, c, di);
+  if (st != W4_OK) return st;
+
+  const int mb = L.M > 8 ? 2 : 1;
+  void* kfn = pick_kernel(L.x_bf16, mb, c.strips, c.row_groups);
+  const int nt = 32 * c.strips;
+  const int rows = L.K / 8;
+
+  CUtensorMap tm_w, tm_s;
+  if (!make_map(&tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, L.packed, (uint64_t)L.N, (uint64_t)rows,
+                32, (uint32_t)(c.row_groups * 16), CU_TENSOR_MAP_SWIZZLE_128B))
+    return fail(W4_ERR_CUDA, "cuTensorMapEncodeTiled failed for packed [%d, %d]", rows, L.N);
+  if (!make_map(&tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.scales, (uint64_t)L.N,
+                (uint64_t)(L.K / 128), (uint32_t)nt, (uint32_t)c.row_groups,
+                CU_TENSOR_MAP_SWIZZLE_NONE))
+    return fail(W4_ERR_CUDA, "cuTensorMapEncodeTiled failed for scales [%d, %d]", L.K / 128,
+                L.N);
+
+  GemvParams p;
+  p.x = L.x;
+  p.y = L.y;
+  p.M = L.M;
+  p.K = L.K;
+  p.N = L.N;
+  p.groups_total = L.K / 128;
+  p.groups_per_split = (p.groups_total + c.split - 1) / c.split;
+  p.stages = c.stages;
+  p.y_bf16 = L.y_bf16;
+  p.err = di.err_word;
+
+  const int threads = (c.strips * c.row_groups + 1) * 32;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((L.N + nt - 1) / nt), (unsigned)c.split, 1);
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
+  cfg.dynamicSmemBytes = gemv_smem_bytes(L.M, L.K, c);
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (c.split > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 1;
+    attrs[na].val.clusterDim.y = (unsigned)c.split;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (c.pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  void* args[] = {&tm_w, &tm_s, &p};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kfn, args);
+  if (e != cudaSuccess) return cuda_fail(e, "w4_gemv launch");
+  return W4_OK;
+}
+
+}  // namespace w4

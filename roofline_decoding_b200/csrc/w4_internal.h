@@ -1,0 +1,57 @@
+// w4_internal.h - declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/w4b200.h"
+
+namespace w4 {
+
+// Records a failure message for w4_last_error() and returns the status.
+int fail(int status, const char* fmt, ...);
+// Converts a CUDA runtime error into W4_ERR_CUDA with a message.
+int cuda_fail(cudaError_t e, const char* what);
+
+// Per-device state filled by w4_init().
+struct DeviceInfo {
+  int sm_count = 0;
+  int max_smem_optin = 0;  // bytes of dynamic shared memory a CTA may opt into
+  int cc_major = 0, cc_minor = 0;
+  int* err_word = nullptr;  // device address of the kernels' error word
+};
+const DeviceInfo& device_info(int device);
+int current_device(int* dev);
+
+// Launchers (no validation: the C ABI layer validates first).
+cudaError_t launch_pack(const void* w, int w_dtype, int32_t* packed, void* scales, int K,
+                        int N, int group_size, cudaStream_t stream);
+cudaError_t launch_dequant(const int32_t* packed, const void* scales, void* out, int out_bf16,
+                           int K, int N, cudaStream_t stream);
+
+struct GemvLaunch {
+  const void* x;
+  const int32_t* packed;
+  const void* scales;
+  void* y;
+  int x_bf16, y_bf16;
+  int M, K, N;
+  w4_gemv_config cfg;
+};
+size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& cfg);
+int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const DeviceInfo& di);
+int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const DeviceInfo& di,
+                       w4_gemv_config* out);
+int launch_gemv(const GemvLaunch& L, cudaStream_t stream);
+int gemv_init_device(const DeviceInfo& di);
+
+// Tensor-map encoder resolved from the driver at init.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn();
+
+}  // namespace w4

@@ -1,0 +1,83 @@
+"""The C ABI library loads and exports every entry point include/w4b200.h declares;
+host-side validation rejects bad arguments before touching a GPU."""
+import ctypes
+import re
+
+import pytest
+
+from roofline_decoding_b200 import _lib
+
+
+def declared_functions():
+    text = _lib.HEADER_PATH.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(w4_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for must in ("w4_pack", "w4_dequant", "w4_gemv", "w4_gemv_ex", "w4_gemv_default_config",
+                 "w4_init", "w4_version", "w4_status_string", "w4_last_error",
+                 "w4_device_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in w4b200.h but not exported"
+    assert set(declared_functions()) <= set(_lib.SIGNATURES)
+
+
+def test_version_and_status_strings():
+    lib = _lib.load()
+    text = _lib.HEADER_PATH.read_text()
+    version = int(re.search(r"#define W4B200_VERSION (\d+)", text).group(1))
+    assert lib.w4_version() == version
+    assert lib.w4_status_string(0) == b"W4_OK"
+    assert lib.w4_status_string(1) == b"W4_ERR_INVALID_ARG"
+    assert lib.w4_status_string(99) == b"W4_ERR_UNKNOWN"
+
+
+def test_validation_happens_before_any_cuda_call():
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    st = lib.w4_gemv(null, 0, null, null, null, 0, 1, 128, 8, 0, 0, null)
+    assert st == _lib.W4_ERR_INVALID_ARG
+    assert b"null pointer" in lib.w4_last_error()
+    fake = ctypes.c_void_p(4096)
+    st = lib.w4_gemv(fake, 0, fake, fake, fake, 0, 1, 100, 8, 0, 0, null)  # K % 128
+    assert st == _lib.W4_ERR_INVALID_ARG
+    st = lib.w4_gemv(fake, 0, fake, fake, fake, 0, 17, 128, 8, 0, 0, null)  # M > 16
+    assert st == _lib.W4_ERR_INVALID_ARG
+    st = lib.w4_gemv(fake, 3, fake, fake, fake, 0, 1, 128, 8, 0, 0, null)  # dtype
+    assert st == _lib.W4_ERR_INVALID_ARG
+    odd = ctypes.c_void_p(4098)
+    st = lib.w4_gemv(odd, 0, fake, fake, fake, 0, 1, 128, 8, 0, 0, null)
+    assert st == _lib.W4_ERR_ALIGNMENT
+    st = lib.w4_pack(fake, 0, fake, fake, 100, 8, 128, null)
+    assert st == _lib.W4_ERR_INVALID_ARG
+    st = lib.w4_dequant(fake, fake, fake, 0, 128, 12, null)  # N % 8
+    assert st == _lib.W4_ERR_INVALID_ARG
+
+
+def test_check_maps_status_to_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.W4_ERR_INVALID_ARG, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.W4_ERR_ALIGNMENT, "x")
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.W4_ERR_UNSUPPORTED, "x")
+    with pytest.raises(_lib.W4Error):
+        _lib.check(_lib.W4_ERR_CUDA, "x")
+    _lib.check(_lib.W4_OK, "x")
+
+
+def test_no_cpu_fallback_in_product_path():
+    """The product package never imports the oracle."""
+    import pathlib
+
+    pkg = pathlib.Path(_lib.__file__).parent
+    for py in pkg.rglob("*.py"):
+        src = py.read_text()
+        assert "oracle" not in re.sub(r"#.*", "", src).replace("the oracle", ""), py

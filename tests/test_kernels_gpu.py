@@ -1,0 +1,340 @@
+"""Parity of the CUDA path (through libw4b200.so's C ABI) with the oracle.
+
+Mirrors the reference's tests/test_kernels.py (pack shapes/dtypes, round trip,
+v1/v2/v3 against x @ dequant(W)) with these bars:
+  * pack and v1 dequantise: bit-exact;
+  * fused GEMV: within rtol = atol = 1e-2 of the reference's
+    dequantise-then-matmul (x.float() @ fp16(dequant).float()), and within
+    the fp32-accumulation + output-rounding budget of the exact sum.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import c_oracle
+from oracle import w4_oracle as o
+
+pytestmark = pytest.mark.gpu
+
+rd = pytest.importorskip("roofline_decoding_b200")
+from roofline_decoding_b200 import kernels as K  # noqa: E402
+from roofline_decoding_b200._lib import GemvConfig  # noqa: E402
+
+DEV = "cuda"
+CONFIG_SHAPES = [(1536, 1536), (1536, 8960), (8960, 1536), (1536, 256), (1024, 1024),
+                 (1024, 2816)]
+REF_TEST_SHAPES = CONFIG_SHAPES[:3] + [(1024, 1024), (1024, 2816), (256, 512)]
+
+
+def sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def gen(Kd, N, kind="normal", seed=0):
+    return o.normal_weights(Kd, N, seed) if kind == "normal" else o.absmax_weights(Kd, N, seed)
+
+
+def to_dev_half(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def to_dev_x(x, bf16):
+    t = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).to(DEV)
+    return t.view(torch.bfloat16) if bf16 else t.view(torch.float16)
+
+
+def pack_dev(w):
+    p, s = K.pack_weights(to_dev_half(w))
+    torch.cuda.synchronize()
+    return p, s
+
+
+def y_tol_exact(y_exact, out_dtype):
+    """fp32 accumulation + one rounding to the output type."""
+    eps = 2.0 ** -8 if out_dtype == torch.bfloat16 else 2.0 ** -11
+    return dict(rtol=eps * 1.01, atol=1e-4 * max(1.0, float(np.abs(y_exact).max())))
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert K.device_error() == 0, "a kernel reported a timed-out wait"
+
+
+# ---------------------------------------------------------------- pack
+
+@pytest.mark.parametrize("name", ["q_proj", "mlp_gate_up", "mlp_down", "kv_proj", "small_attn",
+                                  "small_mlp", "gemm_4096x14336", "ci_256x512", "absmax_q_proj",
+                                  "absmax_mlp_gate", "absmax_mlp_down", "absmax_1024x2816"])
+def test_pack_matches_reference_hashes(golden_hashes, name):
+    c = golden_hashes["cases"][name]
+    p, s = pack_dev(gen(c["K"], c["N"], c["kind"]))
+    assert p.dtype == torch.int32 and s.dtype == torch.float16
+    assert tuple(p.shape) == (c["K"] // 8, c["N"]) and tuple(s.shape) == (c["K"] // 128, c["N"])
+    assert sha(p.cpu().numpy()) == c["packed_sha256"]
+    assert sha(s.cpu().numpy()) == c["scales_sha256"]
+
+
+@pytest.mark.parametrize("name", ["large_8192x28672", "large_28672x8192", "vocab_8192x128256"])
+def test_pack_matches_reference_chunk_hashes(golden_hashes, name):
+    c = golden_hashes["chunked"][name]
+    step = golden_hashes["chunk_n"]
+    p, s = pack_dev(gen(c["K"], c["N"], c["kind"]))
+    p, s = p.cpu().numpy(), s.cpu().numpy()
+    for i, c0 in enumerate(range(0, c["N"], step)):
+        assert sha(p[:, c0:c0 + step]) == c["packed_sha256"][i], f"chunk {i}"
+        assert sha(s[:, c0:c0 + step]) == c["scales_sha256"][i], f"chunk {i}"
+
+
+@pytest.mark.parametrize("case", ["normal_256x512", "absmax_128x64", "normal_1024x96"])
+def test_pack_raw_cases(golden_small, case):
+    p, s = pack_dev(golden_small[f"{case}/w"])
+    np.testing.assert_array_equal(p.cpu().numpy(), golden_small[f"{case}/packed"])
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16),
+                                  golden_small[f"{case}/scales"].view(np.uint16))
+
+
+def test_pack_edge_cases(golden_small):
+    """Ties, subnormals, extremes, underflowing and all-zero groups, inf, NaN.
+
+    Bit-exact with the reference except the nibbles whose quotient is NaN,
+    which hold 0 as torch's cast gives on a CUDA device (the oracle's
+    nan_as='cuda'); the CPU reference stores INT32_MIN there.
+    """
+    w = golden_small["edge/w"]
+    p, s = pack_dev(w)
+    p_o, s_o = o.pack_weights(w, nan_as="cuda")
+    np.testing.assert_array_equal(p.cpu().numpy(), p_o)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), s_o.view(np.uint16))
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16),
+                                  golden_small["edge/scales"].view(np.uint16))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_pack_non_fp16_inputs(dtype):
+    """The reference packs w.float() of any float tensor (kernels.py:34)."""
+    rng = np.random.default_rng(5)
+    w32 = (rng.standard_normal((512, 256)) * 0.03).astype(np.float32)
+    wt = torch.from_numpy(w32).to(DEV).to(dtype)
+    p, s = K.pack_weights(wt)
+    p_o, s_o = o.pack_weights(wt.float().cpu().numpy())
+    np.testing.assert_array_equal(p.cpu().numpy(), p_o)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), s_o.view(np.uint16))
+
+
+def test_pack_cpu_tensor_returns_cpu():
+    w = gen(256, 128)
+    p, s = K.pack_weights(torch.from_numpy(w))
+    assert p.device.type == "cpu" and s.device.type == "cpu"
+    p_o, s_o = o.pack_weights(w)
+    np.testing.assert_array_equal(p.numpy(), p_o)
+
+
+def test_pack_group_size_64():
+    w = gen(256, 64, seed=3)
+    p, s = K.pack_weights(to_dev_half(w), group_size=64)
+    p_o, s_o = o.pack_weights(w, group_size=64)
+    np.testing.assert_array_equal(p.cpu().numpy(), p_o)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), s_o.view(np.uint16))
+
+
+# ---------------------------------------------------------------- dequantize_v1
+
+@pytest.mark.parametrize("Kd,N", REF_TEST_SHAPES)
+@pytest.mark.parametrize("kind", ["normal", "absmax"])
+def test_dequant_v1_bit_exact(Kd, N, kind):
+    w = gen(Kd, N, kind)
+    p, s = pack_dev(w)
+    d = K.dequantize_v1(p, s)
+    assert d.dtype == torch.float16 and tuple(d.shape) == (Kd, N)
+    d_o = o.dequantize_fp16(p.cpu().numpy(), s.cpu().numpy())
+    np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), d_o.view(np.uint16))
+    if kind == "absmax":  # tests/test_kernels.py:32-40
+        assert (d.float() - to_dev_half(w).float()).abs().max().item() < 0.15
+
+
+def test_dequant_v1_bf16_output_bit_exact():
+    p, s = pack_dev(gen(1024, 2816))
+    d = K.dequantize_v1(p, s, out_dtype=torch.bfloat16)
+    bits = d.view(torch.int16).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(bits, o.dequantize_bf16_bits(p.cpu().numpy(),
+                                                               s.cpu().numpy()))
+
+
+# ---------------------------------------------------------------- fused GEMV
+
+def check_gemv(Kd, N, M=1, bf16=False, kind="normal", split_k=None, num_warps=None,
+               out_dtype=None, config=None, seed=0):
+    w = gen(Kd, N, kind, seed)
+    p, s = pack_dev(w)
+    x = o.activations(M, Kd, seed=seed + M, bf16=bf16)
+    xt = to_dev_x(x, bf16)
+    y = K.w4_matmul(xt, p, s, split_k=split_k, num_warps=num_warps, out_dtype=out_dtype,
+                    config=config)
+    out_dtype = out_dtype or torch.float16
+    assert y.dtype == out_dtype and tuple(y.shape) == (M, N)
+    yg = y.float().cpu().numpy()
+    pn, sn = p.cpu().numpy(), s.cpu().numpy()
+    # the reference's dequantise-then-matmul, rtol = atol = 1e-2
+    y_ref = c_oracle.dequant_matmul(x, pn, sn, x_bf16=bf16)
+    np.testing.assert_allclose(yg, y_ref, rtol=1e-2, atol=1e-2)
+    # tight bar: exact sum, fp32 accumulation + one output rounding
+    y_ex = c_oracle.gemv_exact(x, pn, sn, x_bf16=bf16)
+    np.testing.assert_allclose(yg, y_ex, **y_tol_exact(y_ex, out_dtype))
+    return y
+
+
+@pytest.mark.parametrize("Kd,N", CONFIG_SHAPES)
+@pytest.mark.parametrize("bf16", [False, True])
+def test_gemv_v2_config_shapes(Kd, N, bf16):
+    w = gen(Kd, N)
+    p, s = pack_dev(w)
+    x = o.activations(1, Kd, seed=1, bf16=bf16)
+    y = K.gemv_v2(to_dev_x(x, bf16)[0], p, s)
+    assert y.dtype == torch.float16 and tuple(y.shape) == (N,)
+    pn, sn = p.cpu().numpy(), s.cpu().numpy()
+    y_ref = c_oracle.dequant_matmul(x, pn, sn, x_bf16=bf16)[0]
+    np.testing.assert_allclose(y.float().cpu().numpy(), y_ref, rtol=1e-2, atol=1e-2)
+    y_ex = c_oracle.gemv_exact(x, pn, sn, x_bf16=bf16)[0]
+    np.testing.assert_allclose(y.float().cpu().numpy(), y_ex,
+                               **y_tol_exact(y_ex, torch.float16))
+
+
+@pytest.mark.parametrize("Kd,N", REF_TEST_SHAPES)
+def test_gemv_v2_reference_distribution(Kd, N):
+    """tests/test_kernels.py:70-77 on the reference's own weight distribution."""
+    check_gemv(Kd, N, kind="absmax")
+
+
+@pytest.mark.parametrize("Kd,N", [(1536, 1536), (1536, 8960), (256, 512), (8960, 1536)])
+@pytest.mark.parametrize("split_k", [1, 2, 4])
+def test_gemv_v3_split_k(Kd, N, split_k):
+    """tests/test_kernels.py:79-88, with the tight tolerance (no fp16 atomics here)."""
+    w = gen(Kd, N, "absmax")
+    p, s = pack_dev(w)
+    x = o.activations(1, Kd, seed=2)
+    y = K.gemv_v3(to_dev_x(x, False)[0], p, s, split_k=split_k)
+    pn, sn = p.cpu().numpy(), s.cpu().numpy()
+    y_ex = c_oracle.gemv_exact(x, pn, sn)[0]
+    np.testing.assert_allclose(y.float().cpu().numpy(), y_ex, **y_tol_exact(y_ex, torch.float16))
+
+
+def test_gemv_v2_v3_agree():
+    """tests/test_kernels.py:90-95."""
+    w = gen(1024, 2816, "absmax")
+    p, s = pack_dev(w)
+    x = to_dev_x(o.activations(1, 1024, seed=3), False)[0]
+    a = K.gemv_v2(x, p, s).float()
+    b = K.gemv_v3(x, p, s, split_k=1).float()
+    assert torch.allclose(a, b, atol=1e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("split_k", [1, 2, 3, 5, 8, 12, 16])
+@pytest.mark.parametrize("num_warps", [4, 8])
+def test_gemv_every_split_and_warp_count(split_k, num_warps):
+    check_gemv(3072, 512, split_k=split_k, num_warps=num_warps)
+
+
+@pytest.mark.parametrize("strips,row_groups", [(1, 1), (1, 2), (1, 4), (1, 8), (2, 1), (2, 2),
+                                               (2, 4), (4, 1), (4, 2)])
+@pytest.mark.parametrize("stages", [2, 3, 5])
+def test_gemv_every_tile(strips, row_groups, stages):
+    cfg = GemvConfig(strips, row_groups, stages, 2, 0)
+    check_gemv(2048, 640, config=cfg)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 7, 8, 9, 12, 16])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_small_m_gemm(M, bf16):
+    check_gemv(4096, 1024, M=M, bf16=bf16, out_dtype=torch.bfloat16 if bf16 else None)
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16])
+def test_small_m_config5_shape(M):
+    """K=4096, N=14336 at every batch size of the small-M workload."""
+    check_gemv(4096, 14336, M=M, seed=M)
+
+
+@pytest.mark.parametrize("Kd,N", [(128, 8), (128, 24), (256, 40), (384, 200), (1152, 72),
+                                  (128, 4104)])
+def test_ragged_shapes(Kd, N):
+    """Column counts that are not multiples of the 32/64/128-column tiles."""
+    check_gemv(Kd, N)
+    check_gemv(Kd, N, M=3, bf16=True)
+
+
+def test_golden_small_cases(golden_small):
+    for case in ("normal_256x512", "absmax_128x64", "normal_1024x96"):
+        p = to_dev_half(golden_small[f"{case}/packed"])
+        s = to_dev_half(golden_small[f"{case}/scales"])
+        for M in (1, 4):
+            for xdt, bf in (("f16", False), ("bf16", True)):
+                x = to_dev_x(golden_small[f"{case}/x_{xdt}_m{M}"], bf)
+                y = K.w4_matmul(x, p, s).float().cpu().numpy()
+                y_ref = golden_small[f"{case}/y_{xdt}_m{M}"].astype(np.float32)
+                np.testing.assert_allclose(y, y_ref, rtol=1e-2, atol=1e-2)
+
+
+def test_deterministic_across_runs():
+    w = gen(8960, 1536)
+    p, s = pack_dev(w)
+    x = to_dev_x(o.activations(1, 8960, seed=9), False)
+    ys = [K.w4_matmul(x, p, s, split_k=8).clone() for _ in range(5)]
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+
+
+@pytest.mark.parametrize("Kd,N", [(8192, 28672), (28672, 8192), (8192, 128256)])
+def test_large_shapes_against_oracle(Kd, N):
+    """Full-size parity of the multi-GPU workload shapes on one GPU."""
+    check_gemv(Kd, N, seed=11)
+
+
+def test_out_argument_and_bf16_output():
+    p, s = pack_dev(gen(1536, 1536))
+    x = to_dev_x(o.activations(2, 1536, seed=4, bf16=True), True)
+    out = torch.empty((2, 1536), dtype=torch.bfloat16, device=DEV)
+    r = K.w4_matmul(x, p, s, out_dtype=torch.bfloat16, out=out)
+    assert r.data_ptr() == out.data_ptr()
+    y_ex = c_oracle.gemv_exact(x.view(torch.int16).cpu().numpy().view(np.uint16),
+                               p.cpu().numpy(), s.cpu().numpy(), x_bf16=True)
+    np.testing.assert_allclose(out.float().cpu().numpy(), y_ex,
+                               **y_tol_exact(y_ex, torch.bfloat16))
+
+
+# ---------------------------------------------------------------- errors
+
+def test_errors_raise_python_exceptions():
+    p, s = pack_dev(gen(256, 64))
+    x = torch.randn(256, device=DEV, dtype=torch.float16)
+    with pytest.raises(ValueError):
+        K.gemv_v2(torch.randn(200, device=DEV, dtype=torch.float16), p, s)  # wrong K
+    with pytest.raises(ValueError):
+        K.gemv_v2(x.float(), p, s)  # fp32 activations
+    with pytest.raises(ValueError):
+        K.w4_matmul(torch.randn(17, 256, device=DEV, dtype=torch.float16), p, s)  # M > 16
+    with pytest.raises(ValueError):
+        K.gemv_v3(x, p, s, split_k=0)
+    with pytest.raises(ValueError):
+        K.gemv_v3(x, p, s, split_k=3)  # more splits than the 2 K groups
+    with pytest.raises(ValueError):
+        K.gemv_v3(x, p, s, num_warps=2)
+    with pytest.raises(ValueError):
+        K.gemv_v2(x, p, s[:1])  # scales of the wrong shape
+    big = torch.empty(257, device=DEV, dtype=torch.float16)
+    with pytest.raises(ValueError):  # 2-byte offset: misaligned activations
+        K.gemv_v2(big[1:], p, s)
+    with pytest.raises(AssertionError):
+        K.pack_weights(torch.randn(100, 64, device=DEV, dtype=torch.float16))
+
+
+def test_tuner_picks_a_working_config():
+    from roofline_decoding_b200.tuner import tune_gemv
+
+    best, table = tune_gemv(1, 1536, 1536, torch.float16, torch.float16, None, None,
+                            torch.device(DEV), return_table=True)
+    assert len(table) >= 4
+    assert table[0][1] == best.as_tuple()
+    check_gemv(1536, 1536, config=best)
