@@ -296,64 +296,80 @@ def run_ours(args, rank, world, local):
     order = [(K, N, dt) for dt in SWEEP_DTYPES for K, N in SWEEP_SHAPES]
     n_launch = len(order)
 
-    # One graph per timed step (weights of rotation slot step % slots), with an
-    # external timing event after every kernel; read once after the timed run.
-    n_graphs = min(args.steps, 256)
     stream = torch.cuda.Stream(device)
 
-    def launch_all(si, ev=None):
+    def launch_all(si, pdl, ev=None):
         for i, (K, N, dt) in enumerate(order):
             p, s = pool_lookup(pool, si, K, N, dt)
-            Kn.w4_matmul(xs[(K, dt)], p, s, out=ys[(K, N, dt)], config=cfgs[(K, N, dt)])
+            Kn.w4_matmul(xs[(K, dt)], p, s, out=ys[(K, N, dt)], config=cfgs[(K, N, dt)],
+                         pdl=pdl)
             if ev is not None:
                 ev[i + 1].record(stream)
 
     with torch.cuda.stream(stream):
         for si in range(slots):  # warm every buffer once outside capture
-            launch_all(si)
+            launch_all(si, pdl=False)
     stream.synchronize()
-    graphs, evs = [], []
-    for gi in range(n_graphs):
-        ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_launch + 1)]
+
+    # Region A (value): one graph per rotation slot, the 12 GEMVs chained with
+    # programmatic dependent launch, replayed back to back.
+    # Region B (per kernel): the same launches without PDL and with an external
+    # timing event after every kernel, for per-shape times and the roofline.
+    def capture(si, pdl, ev):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
-                ev[0].record(stream)
-                launch_all(gi % slots, ev)
-        graphs.append(g)
-        evs.append(ev)
+                if ev is not None:
+                    ev[0].record(stream)
+                launch_all(si, pdl, ev)
+        return g
+
+    graphs_pdl = [capture(si, True, None) for si in range(slots)]
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_launch + 1)]
+           for _ in range(slots)]
+    graphs_ev = [capture(si, False, evs[si]) for si in range(slots)]
+    with torch.cuda.stream(stream):  # upload every graph before any timing
+        for g in graphs_pdl + graphs_ev:
+            g.replay()
     torch.cuda.synchronize()
 
     copy_gbs = measure_copy_bandwidth_gbs(n_bytes=1 << 30, iters=10, device=device)
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
-            graphs[i % n_graphs].replay()
+            graphs_pdl[i % slots].replay()
     torch.cuda.synchronize()
 
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    per_kernel = [[] for _ in range(n_launch)]
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             start.record(stream)
             for i in range(args.steps):
-                graphs[i % n_graphs].replay()
-                if (i + 1) % n_graphs == 0 and i != args.steps - 1:
-                    stream.synchronize()  # only when steps > 256: read before reuse
-                    for ev in evs:
-                        for k in range(n_launch):
-                            per_kernel[k].append(ev[k].elapsed_time(ev[k + 1]))
+                graphs_pdl[(args.warmup + i) % slots].replay()
             end.record(stream)
         torch.cuda.synchronize()
-    done = args.steps % n_graphs or n_graphs
-    for ev in evs[:done]:
-        for k in range(n_launch):
-            per_kernel[k].append(ev[k].elapsed_time(ev[k + 1]))
-    barrier(world)
-    elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+        barrier(world)
+        elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
+
+        # region B: per-kernel event times, one pass over the slots at a time
+        per_kernel = [[] for _ in range(n_launch)]
+        done = 0
+        with torch.cuda.stream(stream):
+            while done < args.steps:
+                n = min(slots, args.steps - done)
+                for si in range(n):
+                    graphs_ev[si].replay()
+                stream.synchronize()
+                for si in range(n):
+                    for k in range(n_launch):
+                        per_kernel[k].append(evs[si][k].elapsed_time(evs[si][k + 1]))
+                done += n
+        torch.cuda.synchronize()
+    per_kernel = [[max_over_ranks(v, world) for v in ks] for ks in per_kernel] \
+        if world > 1 else per_kernel
 
     bytes_step = sum(gemv_bytes(1, K, N) for K, N, _ in order)
     value = world * bytes_step * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -394,16 +410,19 @@ def run_ours(args, rank, world, local):
                        "l2": f"rotating packed-weight pool of {slots} step copies "
                              f"({slots * 2 * weight_bytes / 2**20:.0f} MiB > 3x L2 "
                              f"{l2 / 2**20:.0f} MiB)",
-                       "timing": "CUDA graph per step, CUDA events, max over ranks"},
-            "gpu_launches": n_launch * args.steps,
+                       "timing": "value: CUDA graph per rotation slot, the 12 GEMVs chained "
+                                 "with programmatic dependent launch, CUDA events around the "
+                                 "steps, max over ranks; per_shape/roofline: the same "
+                                 "launches without PDL, an event after every kernel"},
+            "gpu_launches": n_launch * args.steps,  # region A
             "roofline": {"bound": "hbm", "kernel": f"w4_gemv_kernel K={dK} N={dN} act={ddt}",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": None,
                          "bytes_per_launch": gemv_bytes(1, dK, dN),
                          "mean_launch_us": round(dom_us, 3),
-                         "kernel_time_share_of_step": round(
-                             kernel_total_us / (elapsed_ms * 1e3 / args.steps), 4)},
+                         "sum_isolated_kernel_us_per_step": round(kernel_total_us, 2),
+                         "pdl_chained_us_per_step": round(elapsed_ms * 1e3 / args.steps, 2)},
             "per_shape": per_shape,
             "measured_copy_gbs": round(copy_gbs, 1),
             "e2e": e2e,
@@ -413,7 +432,7 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         line["clocks"] = line_clocks
         print(json.dumps(line), flush=True)
-    del graphs
+    del graphs_pdl, graphs_ev
 
 
 def pool_lookup(pool, si, K, N, dt):

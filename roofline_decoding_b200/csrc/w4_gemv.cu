@@ -160,14 +160,32 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     // x is produced by the previous kernel on the stream: wait for it.
     grid_dependency_wait();
     const uint16_t* xg = static_cast<const uint16_t*>(p.x);
-    for (int idx = threadIdx.x; idx < M * rows_slice; idx += nct) {
-      const int m = idx / rows_slice;
-      const int r = idx - m * rows_slice;
-      const int krow = g0 * 16 + r;  // packed row = 8 activations
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (krow < g1 * 16)
-        v = *reinterpret_cast<const uint4*>(xg + (size_t)m * p.K + (size_t)krow * 8);
-      *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = permute_row(v);
+    // Batches of 4 independent 16-byte loads per thread, all in flight before
+    // the first is consumed (one global round trip per batch, not per row).
+    const int total = M * rows_slice;
+    for (int base = threadIdx.x; base < total; base += 4 * nct) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * nct;
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (idx < total) {
+          const int m = idx / rows_slice;
+          const int krow = g0 * 16 + (idx - m * rows_slice);  // packed row = 8 activations
+          if (krow < g1 * 16)
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(xg + (size_t)m * p.K +
+                                                          (size_t)krow * 8));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * nct;
+        if (idx < total) {
+          const int m = idx / rows_slice;
+          const int r = idx - m * rows_slice;
+          *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = permute_row(v[u]);
+        }
+      }
     }
     consumer_bar_sync(nct);
 
@@ -398,7 +416,10 @@ int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const De
   w4_gemv_config c{sw, rg, 4, split, 0};
   const int gps = (groups + split - 1) / split;
   const int stages_needed = (gps + rg - 1) / rg;
-  c.stages = std::max(2, std::min(4, stages_needed));
+  // Keep the whole share in flight when it is small (each stage that waits
+  // for a free slot costs a DRAM round trip); 6 slots suffice for streaming.
+  c.stages = std::max(2, std::min(6, stages_needed));
+  while (c.stages > 2 && gemv_smem_bytes(M, K, c) > (size_t)di.max_smem_optin / 2) --c.stages;
   // Grow the split until the activation slice fits in shared memory.
   while (gemv_smem_bytes(M, K, c) > (size_t)di.max_smem_optin && c.split < 16 &&
          c.split < groups && split_k <= 0)

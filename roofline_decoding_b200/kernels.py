@@ -25,8 +25,8 @@ from ._lib import GemvConfig, check
 
 GROUP_SIZE = 128  # roofline/kernels.py:21
 
-# Tuned tile per (device name, M, K, N, x dtype, y dtype, split request,
-# warps request) -> GemvConfig tuple. Mirrors roofline/kernels.py:160
+# Tuned tile per (device name, M, K, N, x dtype, split request, warps
+# request) -> GemvConfig tuple. Mirrors roofline/kernels.py:160
 # _TUNE_CACHE, which keyed num_warps by (K, N, split_k).
 _TUNE_CACHE: dict[tuple, tuple[int, int, int, int, int]] = {}
 _TUNE_LOCK = threading.Lock()
@@ -151,8 +151,10 @@ def save_tuned_configs(path: str | os.PathLike | None = None) -> Path:
 
 
 def _tune_key(device, M, K, N, x_dtype, y_dtype, split_k, num_warps) -> tuple:
+    # the output type only changes the final store, so it is not part of the key
+    del y_dtype
     return (_device_key(device), M, K, N, str(x_dtype).replace("torch.", ""),
-            str(y_dtype).replace("torch.", ""), int(split_k or 0), int(num_warps or 0))
+            int(split_k or 0), int(num_warps or 0))
 
 
 def default_config(M: int, K: int, N: int, split_k: int = 0, num_warps: int = 0) -> GemvConfig:

@@ -39,7 +39,9 @@ def _candidates(M: int, K: int, N: int, split_k: int | None, num_warps: int | No
                     continue  # already plenty of CTAs without splitting further
                 gps = -(-groups // split)
                 n_stages = -(-gps // rg)
-                for stages in (2, 3, 4, 6):
+                # up to the whole share in flight at once (small shapes are latency
+                # bound: every stage that waits for a free slot costs a DRAM trip)
+                for stages in (2, 3, 4, 5, 6, 8):
                     if stages > max(2, n_stages):
                         continue
                     c = (strips, rg, stages, split, 0)
@@ -52,7 +54,7 @@ def _candidates(M: int, K: int, N: int, split_k: int | None, num_warps: int | No
 
 
 def time_config(x2, packed, scales, y, cfg: GemvConfig, flush: torch.Tensor,
-                reps: int = 7, warmup: int = 2) -> float:
+                reps: int = 9, warmup: int = 2) -> float:
     """Median device time (us) of one launch with a cold L2."""
     from .kernels import gemv_launch
 
@@ -61,8 +63,8 @@ def time_config(x2, packed, scales, y, cfg: GemvConfig, flush: torch.Tensor,
     for _ in range(warmup):
         gemv_launch(x2, packed, scales, y, cfg)
     for i in range(reps):
-        flush.zero_()
-        starts[i].record()
+        flush.sum()  # evict the weights with clean lines (a write would leave dirty
+        starts[i].record()  # lines whose write-back competes with the timed reads)
         gemv_launch(x2, packed, scales, y, cfg)
         ends[i].record()
     torch.cuda.synchronize()
@@ -71,7 +73,7 @@ def time_config(x2, packed, scales, y, cfg: GemvConfig, flush: torch.Tensor,
 
 def flush_buffer(device: torch.device) -> torch.Tensor:
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    return torch.empty(max(2 * l2, 64 << 20) // 4, dtype=torch.int32, device=device)
+    return torch.zeros(max(2 * l2, 64 << 20) // 4, dtype=torch.float32, device=device)
 
 
 def tune_gemv(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dtype,
@@ -99,3 +101,53 @@ def tune_gemv(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dtype
         table.sort()
         best = GemvConfig.from_tuple(table[0][1])
     return (best, table) if return_table else best
+
+
+# Workload shapes tuned by `python -m roofline_decoding_b200.tuner`:
+# (M, K, N) of the decode sweep, the large multi-GPU shapes (full and per-rank
+# column shards) and the small-M GEMM.
+WORKLOAD_SHAPES = (
+    [(1, k, n) for k, n in [(1536, 1536), (1536, 8960), (8960, 1536), (1536, 256),
+                            (1024, 1024), (1024, 2816), (1536, 2048), (1536, 17920)]]
+    + [(1, k, n // p) for k, n in [(8192, 28672), (28672, 8192), (8192, 128256)]
+       for p in (1, 2, 4, 8)]
+    + [(m, 4096, 14336) for m in (1, 2, 4, 8, 16)]
+)
+
+
+def main(argv=None) -> None:
+    import argparse
+    import json
+
+    from . import kernels
+
+    ap = argparse.ArgumentParser(description="tune the fused GEMV tile per workload shape")
+    ap.add_argument("--out", default=str(kernels.TUNED_CONFIG_PATH))
+    ap.add_argument("--dtypes", default="fp16,bf16")
+    ap.add_argument("--quick", action="store_true", help="decode-sweep shapes only")
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dts = {"fp16": torch.float16, "bf16": torch.bfloat16}
+    shapes = WORKLOAD_SHAPES[:8] if args.quick else WORKLOAD_SHAPES
+    report = []
+    for M, K, N in shapes:
+        for name in args.dtypes.split(","):
+            xdt = dts[name]
+            best, table = tune_gemv(M, K, N, xdt, xdt, None, None, dev, return_table=True)
+            key = kernels._tune_key(dev, M, K, N, xdt, xdt, None, None)
+            kernels._TUNE_CACHE[key] = best.as_tuple()
+            d = kernels.default_config(M, K, N)
+            t_default = next((us for us, c in table if c == d.as_tuple()), None)
+            report.append({"M": M, "K": K, "N": N, "x": name, "best": list(best.as_tuple()),
+                           "best_us": round(table[0][0], 3),
+                           "default": list(d.as_tuple()),
+                           "default_us": None if t_default is None else round(t_default, 3),
+                           "top5": [[round(us, 2), list(c)] for us, c in table[:5]],
+                           "candidates": len(table)})
+            print(json.dumps(report[-1]), flush=True)
+    kernels.save_tuned_configs(args.out)
+    print("saved", args.out)
+
+
+if __name__ == "__main__":
+    main()

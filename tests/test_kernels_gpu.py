@@ -4,8 +4,11 @@ Mirrors the reference's tests/test_kernels.py (pack shapes/dtypes, round trip,
 v1/v2/v3 against x @ dequant(W)) with these bars:
   * pack and v1 dequantise: bit-exact;
   * fused GEMV: within rtol = atol = 1e-2 of the reference's
-    dequantise-then-matmul (x.float() @ fp16(dequant).float()), and within
-    the fp32-accumulation + output-rounding budget of the exact sum.
+    dequantise-then-matmul (x.float() @ fp16(dequant).float()) on the
+    workload's N(0, 0.02) weights (the reference test's own atol = 0.1 on its
+    absmax weights, where the fp16-rounded "want" itself is ~0.02 from the
+    exact sum), and always within the fp32-accumulation + output-rounding
+    budget of the exact sum.
 """
 import hashlib
 
@@ -177,9 +180,13 @@ def check_gemv(Kd, N, M=1, bf16=False, kind="normal", split_k=None, num_warps=No
     assert y.dtype == out_dtype and tuple(y.shape) == (M, N)
     yg = y.float().cpu().numpy()
     pn, sn = p.cpu().numpy(), s.cpu().numpy()
-    # the reference's dequantise-then-matmul, rtol = atol = 1e-2
+    # the reference's dequantise-then-matmul: rtol = atol = 1e-2 on the workload's
+    # N(0, 0.02) weights; on the reference tests' absmax weights (|w| up to 1) its
+    # fp16-rounded "want" is itself up to ~0.02 from the exact sum at K = 8960, so
+    # the reference test's own v2 bar applies there (tests/test_kernels.py:77)
     y_ref = c_oracle.dequant_matmul(x, pn, sn, x_bf16=bf16)
-    np.testing.assert_allclose(yg, y_ref, rtol=1e-2, atol=1e-2)
+    bar = dict(rtol=1e-2, atol=1e-2) if kind == "normal" else dict(rtol=1e-2, atol=0.1)
+    np.testing.assert_allclose(yg, y_ref, **bar)
     # tight bar: exact sum, fp32 accumulation + one output rounding
     y_ex = c_oracle.gemv_exact(x, pn, sn, x_bf16=bf16)
     np.testing.assert_allclose(yg, y_ex, **y_tol_exact(y_ex, out_dtype))
@@ -211,10 +218,18 @@ def test_gemv_v2_reference_distribution(Kd, N):
 @pytest.mark.parametrize("Kd,N", [(1536, 1536), (1536, 8960), (256, 512), (8960, 1536)])
 @pytest.mark.parametrize("split_k", [1, 2, 4])
 def test_gemv_v3_split_k(Kd, N, split_k):
-    """tests/test_kernels.py:79-88, with the tight tolerance (no fp16 atomics here)."""
+    """tests/test_kernels.py:79-88, with the tight tolerance (no fp16 atomics here).
+
+    A split is a whole 128-row group here, so more splits than groups is an
+    argument error (K = 256 has 2 groups).
+    """
     w = gen(Kd, N, "absmax")
     p, s = pack_dev(w)
     x = o.activations(1, Kd, seed=2)
+    if split_k > Kd // 128:
+        with pytest.raises(ValueError):
+            K.gemv_v3(to_dev_x(x, False)[0], p, s, split_k=split_k)
+        return
     y = K.gemv_v3(to_dev_x(x, False)[0], p, s, split_k=split_k)
     pn, sn = p.cpu().numpy(), s.cpu().numpy()
     y_ex = c_oracle.gemv_exact(x, pn, sn)[0]
