@@ -1,31 +1,36 @@
 #!/usr/bin/env python3
 """Benchmark of the W4A16 GEMV path on B200 (one JSON line on rank 0).
 
-Workload (default, --workload sweep): the per-shape batch-1 GEMV sweep of the
-Qwen2.5-1.5B decode layers and the small model's layers: K x N in
-1536x1536 (q/o), 1536x8960 (gate/up), 8960x1536 (down, tall K), 1536x256
-(k/v), 1024x1024, 1024x2816, each with fp16 and bf16 activations, M = 1.
+Workloads (--workload):
+  sweep  (default) the per-shape batch-1 GEMV sweep of the Qwen2.5-1.5B decode
+         layers and the small model's layers: K x N in 1536x1536 (q/o),
+         1536x8960 (gate/up), 8960x1536 (down, tall K), 1536x256 (k/v),
+         1024x1024, 1024x2816, each with fp16 and bf16 activations, M = 1.
+  gemm   small-batch W4A16 GEMM, K=4096, N=14336, M in {1, 2, 4, 8, 16}.
+  large  K=8192,N=28672; K=28672,N=8192; K=8192,N=128256 at M = 1; on N GPUs
+         every rank holds a column slice and an NCCL all-gather assembles y.
+  decode batch-1 greedy decode of a random-init Qwen2.5-1.5B-architecture
+         model (int4 linears, bf16 tied lm_head, static KV 2048), tok/s.
 W ~ N(0, 0.02) fp16 packed to int4 (group 128), x ~ N(0, 1), seeded.
 
-One step = the 12 GEMVs once, each on its own copy of the packed weights; the
-copies rotate so that every launch streams its weights from HBM (the pool is
-larger than 3x the L2). Steps are CUDA graphs (one per rotation slot) with a
-timing event after every kernel, replayed back to back.
-
-  value  : algorithmic bytes of all GEMVs of all ranks / max-over-ranks time
-           of the timed steps, GB/s (inputs resident in HBM).
-  e2e    : the same metric through the public API (w4_matmul) with x copied
-           from pinned host memory and y copied back every GEMV, timed with
-           events around the steps (host synchronises once per step).
-  roofline: the dominant GEMV (largest share of kernel time): algorithmic bytes
-           per launch / its mean event-timed duration, against the measured
-           HBM copy bandwidth in MEASURED_PEAKS.json.
+GEMV workloads: one step = every GEMV of the workload once, each on its own
+copy of the packed weights; copies rotate so that every launch streams its
+weights from HBM (the pool exceeds 3x L2).
+  value   : algorithmic bytes (K*N/2 + 2*N*K/128 + 2*M*K + 2*M*N per GEMV, the
+            full unsharded GEMV) of all ranks / max-over-ranks time, GB/s.
+            Region A: one CUDA graph per rotation slot with the GEMVs chained
+            by programmatic dependent launch, replayed back to back.
+  per_case / roofline: region B, the same launches without PDL and with an
+            event after every kernel; roofline = the GEMV with the largest
+            mean kernel time, bytes per launch / its mean duration, against
+            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  e2e     : the public API (w4_matmul) with x copied from pinned host memory
+            and y copied back for every GEMV, one host sync per step.
   cpu_baseline: the reference's dequantise-then-matmul path restated in C
-           (oracle/w4_oracle.c, OpenMP) on a bounded sample, rank 0 only.
-
+            (oracle/w4_oracle.c, OpenMP) on a bounded sample, rank 0, N = 1.
 --impl reference times that CPU restatement as the reference arm.
-Multi-GPU (torchrun): every rank runs the same sweep on its own GPU (the sweep
-shapes are not partitioned): replicas, weak scaling, no data-path collective.
+Multi-GPU: sweep/gemm/decode run as independent replicas (weak scaling, no
+data-path collective); large is column-parallel (strong scaling).
 """
 from __future__ import annotations
 
@@ -44,13 +49,32 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-SWEEP_SHAPES = [(1536, 1536), (1536, 8960), (8960, 1536), (1536, 256), (1024, 1024),
-                (1024, 2816)]
-SWEEP_DTYPES = ["fp16", "bf16"]
-METRIC = "W4A16 GEMV HBM GB/s (batch-1 per-shape sweep, fp16+bf16 activations)"
-WORKLOAD = ("qwen2.5-1.5b + small-model decode GEMV sweep, M=1: 1536x1536, 1536x8960, "
-            "8960x1536, 1536x256, 1024x1024, 1024x2816; fp16 and bf16 activations")
 FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "sweep": {
+        "cases": [(1, k, n, dt) for dt in ("fp16", "bf16")
+                  for k, n in [(1536, 1536), (1536, 8960), (8960, 1536), (1536, 256),
+                               (1024, 1024), (1024, 2816)]],
+        "metric": "W4A16 GEMV HBM GB/s (batch-1 per-shape sweep, fp16+bf16 activations)",
+        "desc": ("qwen2.5-1.5b + small-model decode GEMV sweep, M=1: 1536x1536, 1536x8960, "
+                 "8960x1536, 1536x256, 1024x1024, 1024x2816; fp16 and bf16 activations"),
+        "sharded": False,
+    },
+    "gemm": {
+        "cases": [(m, 4096, 14336, "fp16") for m in (1, 2, 4, 8, 16)],
+        "metric": "W4A16 small-M GEMM HBM GB/s (K=4096, N=14336, M=1,2,4,8,16)",
+        "desc": "small-batch W4A16 GEMM K=4096 N=14336 at M in {1,2,4,8,16}, fp16 activations",
+        "sharded": False,
+    },
+    "large": {
+        "cases": [(1, 8192, 28672, "fp16"), (1, 28672, 8192, "fp16"), (1, 8192, 128256, "fp16")],
+        "metric": "W4A16 GEMV HBM GB/s (large shapes, column-parallel over GPUs)",
+        "desc": ("Llama-3-70B-like GEMVs M=1: 8192x28672, 28672x8192, vocab 8192x128256; "
+                 "column-sharded with NCCL all-gather when n_gpus > 1"),
+        "sharded": True,
+    },
+}
 
 
 def measured_peaks():
@@ -95,15 +119,16 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(v, world):
+def max_over_ranks(values, world):
+    """Element-wise max over ranks of a list of floats (one collective)."""
     if world == 1:
-        return v
+        return list(values)
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    t = torch.tensor(list(values), dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return t.tolist()
 
 
 # ---------------------------------------------------------------- clocks
@@ -169,43 +194,43 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU baseline
 
-def cpu_cases():
-    """Seeded inputs of the sweep for the CPU restatement (built outside any timing)."""
+def cpu_cases(cases):
+    """Seeded inputs for the CPU restatement (built outside any timing)."""
     from oracle import c_oracle
     from oracle import w4_oracle as o
 
-    cases = []
-    for K, N in SWEEP_SHAPES:
-        w = o.normal_weights(K, N, seed=K * 7 + N)
-        p, s = c_oracle.pack(w)
-        for dt in SWEEP_DTYPES:
-            x = o.activations(1, K, seed=3, bf16=(dt == "bf16"))
-            cases.append((x, p, s, dt == "bf16", np.empty((K, N), dtype=np.uint16),
-                          gemv_bytes(1, K, N)))
-    return cases
+    packs = {}
+    out = []
+    for M, K, N, dt in cases:
+        if (K, N) not in packs:
+            packs[(K, N)] = c_oracle.pack(o.normal_weights(K, N, seed=K * 7 + N))
+        p, s = packs[(K, N)]
+        x = o.activations(M, K, seed=3, bf16=(dt == "bf16"))
+        out.append((x, p, s, dt == "bf16", np.empty((K, N), dtype=np.uint16),
+                    gemv_bytes(M, K, N)))
+    return out
 
 
-def cpu_sweep(cases):
-    """One sweep of the reference's dequantise-then-matmul path on the host cores."""
+def cpu_pass(cases):
+    """One pass of the reference's dequantise-then-matmul path on the host cores."""
     from oracle import c_oracle
 
     for x, p, s, bf, wb, _ in cases:
         c_oracle.dequant_matmul(x, p, s, x_bf16=bf, wbuf=wb)
 
 
-def cpu_sweep_sample(seconds=10.0, min_sweeps=1):
-    """GB/s of the CPU restatement over whole sweeps for about `seconds`."""
+def cpu_sample(cases_spec, seconds):
+    """GB/s of the CPU restatement over whole passes for about `seconds`."""
     from oracle import c_oracle
 
-    cases = cpu_cases()
-    cpu_sweep(cases)  # warm the OpenMP pool and the pages
-    sweeps, t0 = 0, time.perf_counter()
-    while sweeps < min_sweeps or time.perf_counter() - t0 < seconds:
-        cpu_sweep(cases)
-        sweeps += 1
+    cases = cpu_cases(cases_spec)
+    cpu_pass(cases)  # warm the OpenMP pool and the pages
+    passes, t0 = 0, time.perf_counter()
+    while passes < 1 or time.perf_counter() - t0 < seconds:
+        cpu_pass(cases)
+        passes += 1
     dt = time.perf_counter() - t0
-    total = sweeps * sum(c[5] for c in cases)
-    return total / dt / 1e9, sweeps, dt, c_oracle.max_threads()
+    return passes * sum(c[5] for c in cases) / dt / 1e9, passes, dt, c_oracle.max_threads()
 
 
 def run_reference(args, rank, world):
@@ -214,146 +239,147 @@ def run_reference(args, rank, world):
         return
     from oracle import c_oracle
 
-    cases = cpu_cases()
+    wl = WORKLOADS["sweep" if args.workload == "decode" else args.workload]
+    cases = cpu_cases(wl["cases"])
     for _ in range(args.warmup):
-        cpu_sweep(cases)
+        cpu_pass(cases)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_sweep(cases)
+        cpu_pass(cases)
     elapsed = time.perf_counter() - t0
     cores = c_oracle.max_threads()
-    bytes_step = sum(c[5] for c in cases)
-    value = bytes_step * args.steps / elapsed / 1e9
+    value = sum(c[5] for c in cases) * args.steps / elapsed / 1e9
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "impl": "reference", "metric": wl["metric"], "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp32 dequantise-then-matmul)",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": WORKLOAD, "M": 1, "parallelism": "cpu"},
+        "config": {"workload": wl["desc"], "parallelism": "cpu"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores,
                          "kind": "port",
-                         "sample": f"{args.steps} full sweeps (12 GEMVs each), one per step; "
-                                   "oracle/w4_oracle.c dequantise-to-fp16 then fp32 GEMV, "
-                                   "OpenMP"},
+                         "sample": f"{args.steps} passes over the {len(cases)} GEMVs, one per "
+                                   "step; oracle/w4_oracle.c dequantise-to-fp16 then fp32 "
+                                   "GEMV, OpenMP"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------- our arm
+# ---------------------------------------------------------------- GEMV workloads
 
-def build_cases(torch, device, pool_min_bytes):
-    from roofline_decoding_b200 import kernels as Kn
-
+def build_pool(torch, Kn, cases, device, rank, world, sharded):
+    """Packed weights per case, rotated over enough copies to exceed 3x L2."""
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    base = []
-    for K, N in SWEEP_SHAPES:
-        g = torch.Generator(device="cpu").manual_seed(K * 7 + N)
-        w = (torch.randn((K, N), generator=g) * 0.02).half().to(device)
-        p, s = Kn.pack_weights(w)
-        base.append((K, N, p, s))
+    base = {}
+    for M, K, N, dt in cases:
+        if (K, N) in base:
+            continue
+        n_loc = N // world if sharded else N
+        g = torch.Generator(device=device).manual_seed(K * 7 + N + 1000 * rank)
+        w = (torch.randn((K, n_loc), generator=g, device=device) * 0.02).half()
+        base[(K, N)] = Kn.pack_weights(w)
         del w
-    weight_bytes = sum(p.numel() * 4 + s.numel() * 2 for _, _, p, s in base)
-    # each step uses 2 copies (one per activation dtype); rotate over enough
-    # copies that the pool exceeds 3x L2
-    slots = max(2, -(-max(3 * l2, pool_min_bytes) // (2 * weight_bytes)))
+    step_bytes = sum(p.numel() * 4 + s.numel() * 2 for M, K, N, dt in cases
+                     for p, s in [base[(K, N)]])
+    slots = max(2, -(-3 * l2 // step_bytes))
     pool = []
-    for _ in range(slots):
+    for si in range(slots):
         slot = []
-        for dt in SWEEP_DTYPES:
-            slot.append([(K, N, p.clone(), s.clone()) for K, N, p, s in base])
+        for M, K, N, dt in cases:
+            p, s = base[(K, N)]
+            slot.append((p.clone(), s.clone()) if si else (p, s))
         pool.append(slot)
-    xs = {}
-    for K, _ in SWEEP_SHAPES:
-        for dt in SWEEP_DTYPES:
-            tdt = torch.float16 if dt == "fp16" else torch.bfloat16
-            g = torch.Generator(device="cpu").manual_seed(K)
-            xs[(K, dt)] = torch.randn((1, K), generator=g).to(tdt).to(device)
-    return pool, xs, slots, weight_bytes, l2
+    return pool, slots, step_bytes, l2
 
 
-def run_ours(args, rank, world, local):
+def run_gemv_workload(args, rank, world, local):
     import torch
 
     from roofline_decoding_b200 import kernels as Kn
     from roofline_decoding_b200.roofline import measure_copy_bandwidth_gbs
 
+    wl = WORKLOADS[args.workload]
+    cases = wl["cases"]
+    sharded = wl["sharded"] and world > 1
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peak, peak_kind = measured_peaks()
-    pool, xs, slots, weight_bytes, l2 = build_cases(torch, device, 0)
     tdt = {"fp16": torch.float16, "bf16": torch.bfloat16}
-    ys = {(K, N, dt): torch.empty((1, N), dtype=torch.float16, device=device)
-          for K, N in SWEEP_SHAPES for dt in SWEEP_DTYPES}
-    # tune (or load) the tile of every shape before any capture
-    cfgs = {}
-    for K, N in SWEEP_SHAPES:
-        for dt in SWEEP_DTYPES:
-            cfgs[(K, N, dt)] = Kn.tuned_config(1, K, N, tdt[dt], torch.float16, None, None,
-                                               device)
-    order = [(K, N, dt) for dt in SWEEP_DTYPES for K, N in SWEEP_SHAPES]
-    n_launch = len(order)
-
+    pool, slots, step_bytes, l2 = build_pool(torch, Kn, cases, device, rank, world, sharded)
+    n_loc = [N // world if sharded else N for M, K, N, dt in cases]
+    xs = []
+    for M, K, N, dt in cases:
+        g = torch.Generator(device="cpu").manual_seed(K + M)
+        xs.append(torch.randn((M, K), generator=g).to(tdt[dt]).to(device))
+    ys = [torch.empty((M, n), dtype=torch.float16, device=device)
+          for (M, K, N, dt), n in zip(cases, n_loc)]
+    gathered = [torch.empty((world * M, n), dtype=torch.float16, device=device)
+                for (M, K, N, dt), n in zip(cases, n_loc)] if sharded else None
+    cfgs = [Kn.tuned_config(M, K, n, tdt[dt], torch.float16, None, None, device)
+            for (M, K, N, dt), n in zip(cases, n_loc)]
+    n_launch = len(cases)
     stream = torch.cuda.Stream(device)
 
-    def launch_all(si, pdl, ev=None):
-        for i, (K, N, dt) in enumerate(order):
-            p, s = pool_lookup(pool, si, K, N, dt)
-            Kn.w4_matmul(xs[(K, dt)], p, s, out=ys[(K, N, dt)], config=cfgs[(K, N, dt)],
-                         pdl=pdl)
+    def launch_all(si, pdl, ev=None, gather=True):
+        for i in range(n_launch):
+            p, s = pool[si][i]
+            Kn.w4_matmul(xs[i], p, s, out=ys[i], config=cfgs[i], pdl=pdl)
             if ev is not None:
                 ev[i + 1].record(stream)
+        if sharded and gather:
+            import torch.distributed as dist
+
+            for i in range(n_launch):
+                dist.all_gather_into_tensor(gathered[i], ys[i])
 
     with torch.cuda.stream(stream):
         for si in range(slots):  # warm every buffer once outside capture
             launch_all(si, pdl=False)
     stream.synchronize()
 
-    # Region A (value): one graph per rotation slot, the 12 GEMVs chained with
-    # programmatic dependent launch, replayed back to back.
-    # Region B (per kernel): the same launches without PDL and with an external
-    # timing event after every kernel, for per-shape times and the roofline.
-    def capture(si, pdl, ev):
+    def capture(si, pdl, ev, gather=True):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
                 if ev is not None:
                     ev[0].record(stream)
-                launch_all(si, pdl, ev)
+                launch_all(si, pdl, ev, gather)
         return g
 
     graphs_pdl = [capture(si, True, None) for si in range(slots)]
+    graphs_gemv = [capture(si, True, None, gather=False) for si in range(slots)] \
+        if sharded else []
     evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_launch + 1)]
            for _ in range(slots)]
-    graphs_ev = [capture(si, False, evs[si]) for si in range(slots)]
+    graphs_ev = [capture(si, False, evs[si], gather=False) for si in range(slots)]
     with torch.cuda.stream(stream):  # upload every graph before any timing
-        for g in graphs_pdl + graphs_ev:
+        for g in graphs_pdl + graphs_ev + graphs_gemv:
             g.replay()
     torch.cuda.synchronize()
 
     copy_gbs = measure_copy_bandwidth_gbs(n_bytes=1 << 30, iters=10, device=device)
 
+    def timed(graphs, steps, offset):
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            s_ev.record(stream)
+            for i in range(steps):
+                graphs[(offset + i) % slots].replay()
+            e_ev.record(stream)
+        torch.cuda.synchronize()
+        return s_ev.elapsed_time(e_ev)
+
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
             graphs_pdl[i % slots].replay()
     torch.cuda.synchronize()
-
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for i in range(args.steps):
-                graphs_pdl[(args.warmup + i) % slots].replay()
-            end.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        elapsed_ms = max_over_ranks(start.elapsed_time(end), world)
-
+        ms_a = timed(graphs_pdl, args.steps, args.warmup)
+        ms_gemv = timed(graphs_gemv, args.steps, args.warmup) if sharded else 0.0
         # region B: per-kernel event times, one pass over the slots at a time
         per_kernel = [[] for _ in range(n_launch)]
         done = 0
@@ -368,95 +394,93 @@ def run_ours(args, rank, world, local):
                         per_kernel[k].append(evs[si][k].elapsed_time(evs[si][k + 1]))
                 done += n
         torch.cuda.synchronize()
-    per_kernel = [[max_over_ranks(v, world) for v in ks] for ks in per_kernel] \
-        if world > 1 else per_kernel
+    elapsed_ms, ms_gemv = max_over_ranks([ms_a, ms_gemv], world)
+    mean_k = max_over_ranks([statistics.mean(v) for v in per_kernel], world)
 
-    bytes_step = sum(gemv_bytes(1, K, N) for K, N, _ in order)
-    value = world * bytes_step * args.steps / (elapsed_ms / 1e3) / 1e9
+    full_bytes = [gemv_bytes(M, K, N) for M, K, N, dt in cases]
+    local_bytes = [gemv_bytes(M, K, n) for (M, K, N, dt), n in zip(cases, n_loc)]
+    bytes_step = sum(full_bytes) if sharded else sum(full_bytes) * world
+    value = bytes_step * args.steps / (elapsed_ms / 1e3) / 1e9
 
-    # per-shape table and the dominant kernel
-    per_shape = []
-    for k, (K, N, dt) in enumerate(order):
-        t_us = statistics.mean(per_kernel[k]) * 1e3
-        gbs = gemv_bytes(1, K, N) / (t_us * 1e-6) / 1e9
-        per_shape.append({"K": K, "N": N, "act": dt, "us": round(t_us, 2),
-                          "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
-                          "config": list(cfgs[(K, N, dt)].as_tuple())})
-    dom = max(range(n_launch), key=lambda k: sum(per_kernel[k]))
-    dK, dN, ddt = order[dom]
-    dom_us = statistics.mean(per_kernel[dom]) * 1e3
-    achieved = gemv_bytes(1, dK, dN) / (dom_us * 1e-6) / 1e9
-    kernel_total_us = sum(statistics.mean(v) * 1e3 for v in per_kernel)
+    per_case = []
+    for k, (M, K, N, dt) in enumerate(cases):
+        t_us = mean_k[k] * 1e3
+        gbs = local_bytes[k] / (t_us * 1e-6) / 1e9
+        per_case.append({"M": M, "K": K, "N": N, "N_local": n_loc[k], "act": dt,
+                         "us": round(t_us, 2), "GBps": round(gbs, 1),
+                         "frac": round(gbs / peak, 4), "config": list(cfgs[k].as_tuple())})
+    dom = max(range(n_launch), key=lambda k: mean_k[k])
+    dM, dK, dN, ddt = cases[dom]
+    dom_us = mean_k[dom] * 1e3
+    achieved = local_bytes[dom] / (dom_us * 1e-6) / 1e9
 
-    # e2e through the public API with host buffers
-    e2e = run_e2e(torch, Kn, pool, cfgs, order, args, device, world)
-
-    line = None
+    e2e = run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered,
+                  n_loc)
+    clk = clocks.summary()
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            v, sweeps, dt_s, cores = cpu_sweep_sample(seconds=args.cpu_seconds)
+            v, passes, dt_s, cores = cpu_sample(cases, args.cpu_seconds)
             cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                   "sample": f"{sweeps} full sweeps (12 GEMVs) in {dt_s:.1f} s of "
+                   "sample": f"{passes} passes over the {len(cases)} GEMVs in {dt_s:.1f} s of "
                              "oracle/w4_oracle.c dequantise-to-fp16 then fp32 GEMV, OpenMP"}
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "metric": wl["metric"], "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(elapsed_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp32 accumulate)",
+            "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+            "dtype": "w4a16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) weights packed to int4, N(0,1) activations)",
-            "config": {"workload": WORKLOAD, "M": 1, "global_batch": world,
-                       "parallelism": f"replicas{world}",
-                       "l2": f"rotating packed-weight pool of {slots} step copies "
-                             f"({slots * 2 * weight_bytes / 2**20:.0f} MiB > 3x L2 "
-                             f"{l2 / 2**20:.0f} MiB)",
-                       "timing": "value: CUDA graph per rotation slot, the 12 GEMVs chained "
-                                 "with programmatic dependent launch, CUDA events around the "
-                                 "steps, max over ranks; per_shape/roofline: the same "
-                                 "launches without PDL, an event after every kernel"},
-            "gpu_launches": n_launch * args.steps,  # region A
-            "roofline": {"bound": "hbm", "kernel": f"w4_gemv_kernel K={dK} N={dN} act={ddt}",
+            "config": {"workload": wl["desc"], "global_batch": 1 if sharded else world,
+                       "parallelism": (f"column-parallel{world} + NCCL all-gather" if sharded
+                                       else f"replicas{world}"),
+                       "l2": (f"rotating packed-weight pool of {slots} step copies "
+                              f"({slots * step_bytes / 2**20:.0f} MiB >= 3x L2 "
+                              f"{l2 / 2**20:.0f} MiB)"),
+                       "timing": "value: CUDA graph per rotation slot, GEMVs chained with "
+                                 "programmatic dependent launch, events around the steps, "
+                                 "max over ranks; per_case/roofline: the same launches "
+                                 "without PDL, an event after every kernel"},
+            "gpu_launches": n_launch * args.steps,
+            "roofline": {"bound": "hbm",
+                         "kernel": f"w4_gemv_kernel M={dM} K={dK} N={n_loc[dom]} act={ddt}",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": None,
-                         "bytes_per_launch": gemv_bytes(1, dK, dN),
+                         "traffic": None, "bytes_per_launch": local_bytes[dom],
                          "mean_launch_us": round(dom_us, 3),
-                         "sum_isolated_kernel_us_per_step": round(kernel_total_us, 2),
+                         "sum_isolated_kernel_us_per_step": round(sum(mean_k) * 1e3, 2),
                          "pdl_chained_us_per_step": round(elapsed_ms * 1e3 / args.steps, 2)},
-            "per_shape": per_shape,
+            "per_case": per_case,
             "measured_copy_gbs": round(copy_gbs, 1),
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "clocks": clk,
         }
-    line_clocks = clocks.summary()
-    if rank == 0:
-        line["clocks"] = line_clocks
+        if sharded:
+            line["gemv_only_ms_per_step"] = round(ms_gemv / args.steps, 4)
+            line["gather_ms_per_step"] = round((elapsed_ms - ms_gemv) / args.steps, 4)
         print(json.dumps(line), flush=True)
-    del graphs_pdl, graphs_ev
+    del graphs_pdl, graphs_ev, graphs_gemv  # graphs holding NCCL calls go first
 
 
-def pool_lookup(pool, si, K, N, dt):
-    for k2, n2, p, s in pool[si][SWEEP_DTYPES.index(dt)]:
-        if (k2, n2) == (K, N):
-            return p, s
-    raise KeyError((K, N, dt))
-
-
-def run_e2e(torch, Kn, pool, cfgs, order, args, device, world):
-    """Public-API steps: pinned x -> device, fused GEMV, y -> pinned host, per GEMV."""
-    hx, hy = {}, {}
-    for K, N, dt in order:
-        tdt = torch.float16 if dt == "fp16" else torch.bfloat16
-        hx[(K, N, dt)] = torch.randn((1, K)).to(tdt).pin_memory()
-        hy[(K, N, dt)] = torch.empty((1, N), dtype=torch.float16).pin_memory()
+def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered, n_loc):
+    """Public-API steps: pinned x -> device, fused GEMV(s), y -> pinned host."""
+    hx = [x.cpu().pin_memory() for x in xs]
+    hy = [torch.empty((M * world if sharded else M, n), dtype=torch.float16).pin_memory()
+          for (M, K, N, dt), n in zip(cases, n_loc)]
     slots = len(pool)
 
     def step(i):
-        for K, N, dt in order:
-            p, s = pool_lookup(pool, i % slots, K, N, dt)
-            xd = hx[(K, N, dt)].to(device, non_blocking=True)
-            y = Kn.w4_matmul(xd, p, s, config=cfgs[(K, N, dt)])
-            hy[(K, N, dt)].copy_(y, non_blocking=True)
+        for k in range(len(cases)):
+            p, s = pool[i % slots][k]
+            xd = hx[k].to(device, non_blocking=True)
+            y = Kn.w4_matmul(xd, p, s, config=cfgs[k])
+            if sharded:
+                import torch.distributed as dist
+
+                dist.all_gather_into_tensor(gathered[k], y)
+                y = gathered[k]
+            hy[k].copy_(y, non_blocking=True)
         torch.cuda.current_stream(device).synchronize()
 
     for i in range(args.warmup):
@@ -469,15 +493,98 @@ def run_e2e(torch, Kn, pool, cfgs, order, args, device, world):
         step(args.warmup + i)
     e_ev.record()
     torch.cuda.synchronize()
-    ms = max_over_ranks(s_ev.elapsed_time(e_ev), world)
-    bytes_step = sum(gemv_bytes(1, K, N) for K, N, _ in order)
-    h2d = sum(hx[k].numel() * hx[k].element_size() for k in hx)
-    d2h = sum(hy[k].numel() * hy[k].element_size() for k in hy)
-    return {"value": round(world * bytes_step * args.steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+    ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
+    full = sum(gemv_bytes(M, K, N) for M, K, N, dt in cases)
+    bytes_step = full if sharded else full * world
+    return {"value": round(bytes_step * args.steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in hx),
+            "d2h_bytes_per_step": sum(y.numel() * y.element_size() for y in hy),
             "ms_per_step": round(ms / args.steps, 4),
-            "path": "roofline_decoding_b200.w4_matmul (C ABI w4_gemv_ex) per GEMV, "
-                    "pinned H2D x, D2H y, one host sync per step"}
+            "path": "roofline_decoding_b200.w4_matmul (C ABI w4_gemv_ex) per GEMV, pinned "
+                    "H2D x, D2H y, one host sync per step"}
+
+
+# ---------------------------------------------------------------- decode workload
+
+def run_decode(args, rank, world, local):
+    import torch
+
+    from roofline_decoding_b200.decode import W4DecodeModel
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peak, peak_kind = measured_peaks()
+    model = W4DecodeModel(device=device, seed=0)
+    model.capture()
+    prompt_len = 32
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g)
+    if prompt_len + args.warmup + args.steps > model.cfg.max_seq:
+        raise SystemExit("prompt + warmup + steps exceed the 2048-token KV cache")
+    model.set_prompt(prompt)
+    for _ in range(prompt_len + args.warmup):
+        model.graph.replay()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        s_ev.record()
+        for _ in range(args.steps):
+            model.graph.replay()
+        e_ev.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
+    tok_s = world * args.steps / (ms / 1e3)
+    step_bytes = model.bytes_per_step()  # the attention reads the whole static cache
+    achieved = step_bytes * (args.steps / (ms / 1e3)) / 1e9
+
+    # e2e: a host-driven loop that reads every token (like .item() per token)
+    # and writes it back as the next step's input
+    host_tok = torch.zeros((1,), dtype=torch.long).pin_memory()
+    model.set_prompt(prompt)
+    for _ in range(prompt_len + args.warmup):
+        model.graph.replay()
+    host_tok.copy_(model.token)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        model.token.copy_(host_tok, non_blocking=True)
+        model.graph.replay()
+        host_tok.copy_(model.token, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2.record()
+    torch.cuda.synchronize()
+    ms2 = max_over_ranks([s2.elapsed_time(e2)], world)[0]
+    clk = clocks.summary()
+    if rank != 0:
+        return
+    line = {
+        "metric": "batch-1 greedy decode tok/s (W4A16 Qwen2.5-1.5B architecture, CUDA graph)",
+        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "w4a16 linears, bf16 activations/lm_head",
+        "data": "synthetic (random-init seeded weights, 32 random prompt ids)",
+        "config": {"workload": "Qwen2.5-1.5B architecture decode, 28 layers, hidden 1536, "
+                               "int4 linears, tied bf16 lm_head 1536x151936, static KV 2048",
+                   "prompt": prompt_len, "global_batch": world,
+                   "parallelism": f"replicas{world}"},
+        "gpu_launches": None,
+        "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": None, "bytes_per_step": step_bytes,
+                     "ceiling_tok_s": round(peak * 1e9 / step_bytes, 1)},
+        "e2e": {"value": round(world * args.steps / (ms2 / 1e3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
+                "ms_per_step": round(ms2 / args.steps, 4),
+                "path": "W4DecodeModel graph replay, token H2D + D2H and a host sync per step"},
+        "cpu_baseline": None,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -486,6 +593,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode"], default="sweep")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -495,8 +603,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload == "decode":
+            run_decode(args, rank, world, local)
         else:
-            run_ours(args, rank, world, local)
+            run_gemv_workload(args, rank, world, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -110,6 +110,64 @@ int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed,
 int w4_gemv_default_config(int M, int K, int N, int split_k, int num_warps,
                            w4_gemv_config* out);
 
+/* Operations fused into the GEMV for a decode step. */
+typedef enum { W4_PRO_NONE = 0, W4_PRO_RMSNORM = 1, W4_PRO_SWIGLU = 2 } w4_prologue;
+typedef enum { W4_EPI_NONE = 0, W4_EPI_BIAS = 1, W4_EPI_RESIDUAL = 2 } w4_epilogue;
+typedef struct {
+  int prologue;            /* W4_PRO_RMSNORM: x <- rmsnorm(x) * norm_weight;
+                              W4_PRO_SWIGLU : x is [M, 2K] gate|up, x <- silu(gate) * up */
+  const void* norm_weight; /* RMSNorm weight [K] (x's type), 16-byte aligned */
+  float eps;               /* RMSNorm epsilon */
+  int epilogue;            /* W4_EPI_BIAS: y <- y + bias[n];
+                              W4_EPI_RESIDUAL: y <- residual + round(y) (may alias y) */
+  const void* epi_src;     /* bias [N] or residual [M, N] (y's type) */
+} w4_fused_ops;
+
+/* w4_gemv_ex with fused prologue/epilogue (the decoder layer's RMSNorm,
+ * SwiGLU, q/k/v bias and residual adds of scripts/decode_loop.py's HF
+ * forward, which ran them as separate torch ops around W4Linear). */
+int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed,
+                  const void* scales, void* y, int y_dtype, int M, int K, int N,
+                  const w4_fused_ops* ops, const w4_gemv_config* cfg,
+                  void* stream);
+
+/* Decode-step kernels (bf16 activations), the rest of the batch-1 greedy
+ * step that scripts/decode_loop.py:106-124 ran as an HF forward. All read
+ * the step state (token, position) from device memory, so a whole step can
+ * be captured once in a CUDA graph; pdl != 0 launches them with
+ * programmatic dependent launch.
+ *
+ * w4_decode_embed: token <- pos < prompt_len ? prompt[pos] : token;
+ *   h[hidden] <- embed[token, :]. */
+int w4_decode_embed(const void* embed, int vocab, int hidden,
+                    const int64_t* prompt, const int64_t* prompt_len,
+                    int64_t* token, const int64_t* pos, void* h, int pdl,
+                    void* stream);
+
+/* w4_decode_attention: RoPE (rotate-half; cos/sin tables [max_seq,
+ * head_dim]) on q and k of qkv = [q (heads*hd) | k (kv*hd) | v (kv*hd)],
+ * k and v stored at position pos of the layer's caches [kv, max_seq, hd],
+ * then GQA attention of every q head over positions 0..pos with softmax in
+ * fp32; out [heads*hd]. head_dim must be 128. */
+int w4_decode_attention(const void* qkv, const void* cos_table,
+                        const void* sin_table, const int64_t* pos,
+                        void* k_cache, void* v_cache, void* out, int heads,
+                        int kv_heads, int head_dim, int max_seq, int pdl,
+                        void* stream);
+
+/* Workspace bytes w4_lm_head_argmax needs (zeroed once by the caller). */
+size_t w4_lm_head_workspace_bytes(void);
+
+/* w4_lm_head_argmax: x = rmsnorm(h) * norm_weight, logits[v] = embed[v, :]
+ * . x (bf16, the tied embedding as lm_head), token <- argmax (first index
+ * among equal bf16 logits, like torch.argmax), pos <- pos + 1. logits may be
+ * NULL. The workspace (w4_lm_head_workspace_bytes, zeroed before the first
+ * call) carries the cross-CTA argmax and is left zeroed again. */
+int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps,
+                      const void* embed, int vocab, int hidden, void* logits,
+                      int64_t* token, int64_t* pos, void* workspace,
+                      size_t workspace_bytes, int pdl, void* stream);
+
 /* Reads and clears the device-side error word that kernels set when a
  * bounded wait gives up (0 = no error). Synchronises the device. */
 int w4_device_error(int device, int* code);

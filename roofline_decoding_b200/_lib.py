@@ -47,6 +47,21 @@ class GemvConfig(ctypes.Structure):
                 % self.as_tuple())
 
 
+W4_PRO_NONE, W4_PRO_RMSNORM, W4_PRO_SWIGLU = 0, 1, 2
+W4_EPI_NONE, W4_EPI_BIAS, W4_EPI_RESIDUAL = 0, 1, 2
+
+
+class FusedOps(ctypes.Structure):
+    """w4_fused_ops: prologue/epilogue fused into the GEMV (include/w4b200.h)."""
+    _fields_ = [
+        ("prologue", ctypes.c_int),
+        ("norm_weight", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("epilogue", ctypes.c_int),
+        ("epi_src", ctypes.c_void_p),
+    ]
+
+
 _c_int, _c_void_p, _c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
 # name -> (restype, argtypes); must match include/w4b200.h
@@ -64,6 +79,18 @@ SIGNATURES = {
                             _c_int, _c_int, ctypes.POINTER(GemvConfig), _c_void_p]),
     "w4_gemv_default_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int,
                                         ctypes.POINTER(GemvConfig)]),
+    "w4_gemv_fused": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
+                               _c_int, _c_int, _c_int, ctypes.POINTER(FusedOps),
+                               ctypes.POINTER(GemvConfig), _c_void_p]),
+    "w4_decode_embed": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+                                 _c_void_p, _c_void_p, _c_int, _c_void_p]),
+    "w4_decode_attention": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                     _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int,
+                                     _c_int, _c_void_p]),
+    "w4_lm_head_workspace_bytes": (_c_size_t, []),
+    "w4_lm_head_argmax": (_c_int, [_c_void_p, _c_void_p, ctypes.c_float, _c_void_p, _c_int,
+                                   _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                   _c_size_t, _c_int, _c_void_p]),
     "w4_device_error": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
 }
 

@@ -90,6 +90,7 @@ int init_locked(int device) {
     }
     di.err_word = static_cast<int*>(addr);
     st = gemv_init_device(di);
+    if (st == W4_OK) st = decode_init_device(di);
   } while (false);
   if (prev != device) cudaSetDevice(prev);
   if (st == W4_OK) {
@@ -209,7 +210,7 @@ int w4_gemv(const void* x, int x_dtype, const int32_t* packed, const void* scale
   if (st != W4_OK) return st;
   w4_gemv_config c;
   if ((st = w4_gemv_default_config(M, K, N, split_k, num_warps, &c)) != W4_OK) return st;
-  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, c};
+  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, c, {}};
   return launch_gemv(L, (cudaStream_t)stream);
 }
 
@@ -218,8 +219,86 @@ int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed, const void* sc
   int st = gemv_check(x, x_dtype, packed, scales, y, y_dtype, M, K, N);
   if (st != W4_OK) return st;
   if (!cfg) return fail(W4_ERR_INVALID_ARG, "w4_gemv_ex: null config");
-  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg};
+  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg, {}};
   return launch_gemv(L, (cudaStream_t)stream);
+}
+
+int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void* scales,
+                  void* y, int y_dtype, int M, int K, int N, const w4_fused_ops* ops,
+                  const w4_gemv_config* cfg, void* stream) {
+  int st = gemv_check(x, x_dtype, packed, scales, y, y_dtype, M, K, N);
+  if (st != W4_OK) return st;
+  if (!cfg || !ops) return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: null config or ops");
+  if (ops->prologue < W4_PRO_NONE || ops->prologue > W4_PRO_SWIGLU)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: prologue %d unknown", ops->prologue);
+  if (ops->epilogue < W4_EPI_NONE || ops->epilogue > W4_EPI_RESIDUAL)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: epilogue %d unknown", ops->epilogue);
+  if (ops->prologue == W4_PRO_RMSNORM && (!ops->norm_weight || !aligned16(ops->norm_weight)))
+    return fail(W4_ERR_ALIGNMENT, "w4_gemv_fused: RMSNorm weight missing or not 16-byte aligned");
+  if (ops->prologue != W4_PRO_NONE && x_dtype != y_dtype)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: a prologue needs x and y of one type");
+  if (ops->epilogue != W4_EPI_NONE && !ops->epi_src)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: epilogue source missing");
+  GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg,
+               *ops};
+  return launch_gemv(L, (cudaStream_t)stream);
+}
+
+int w4_decode_embed(const void* embed, int vocab, int hidden, const int64_t* prompt,
+                    const int64_t* prompt_len, int64_t* token, const int64_t* pos, void* h,
+                    int pdl, void* stream) {
+  if (!embed || !prompt || !prompt_len || !token || !pos || !h)
+    return fail(W4_ERR_INVALID_ARG, "w4_decode_embed: null pointer");
+  if (vocab <= 0 || hidden <= 0 || hidden % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_decode_embed: vocab=%d hidden=%d", vocab, hidden);
+  if (!aligned16(embed) || !aligned16(h))
+    return fail(W4_ERR_ALIGNMENT, "w4_decode_embed: embed/h must be 16-byte aligned");
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  return launch_decode_embed(embed, vocab, hidden, prompt, prompt_len, token, pos, h, pdl,
+                             (cudaStream_t)stream);
+}
+
+int w4_decode_attention(const void* qkv, const void* cos_table, const void* sin_table,
+                        const int64_t* pos, void* k_cache, void* v_cache, void* out, int heads,
+                        int kv_heads, int head_dim, int max_seq, int pdl, void* stream) {
+  if (!qkv || !cos_table || !sin_table || !pos || !k_cache || !v_cache || !out)
+    return fail(W4_ERR_INVALID_ARG, "w4_decode_attention: null pointer");
+  if (head_dim != 128)
+    return fail(W4_ERR_UNSUPPORTED, "w4_decode_attention: head_dim %d (128 only)", head_dim);
+  if (kv_heads <= 0 || heads <= 0 || heads % kv_heads != 0 || heads / kv_heads > 16)
+    return fail(W4_ERR_INVALID_ARG, "w4_decode_attention: heads=%d kv_heads=%d", heads, kv_heads);
+  if (max_seq <= 0 || max_seq > 16384)
+    return fail(W4_ERR_INVALID_ARG, "w4_decode_attention: max_seq=%d outside 1..16384", max_seq);
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  return launch_decode_attention(qkv, cos_table, sin_table, pos, k_cache, v_cache, out, heads,
+                                 kv_heads, max_seq, pdl, (cudaStream_t)stream);
+}
+
+size_t w4_lm_head_workspace_bytes(void) { return lm_head_workspace_bytes(); }
+
+int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps, const void* embed,
+                      int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
+                      void* workspace, size_t workspace_bytes, int pdl, void* stream) {
+  if (!h || !norm_weight || !embed || !token || !pos || !workspace)
+    return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax: null pointer");
+  if (workspace_bytes < lm_head_workspace_bytes())
+    return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax: workspace of %zu bytes < %zu",
+                workspace_bytes, lm_head_workspace_bytes());
+  if (vocab <= 0 || hidden % 256 != 0 || hidden < 256 || hidden > 4096)
+    return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden=%d (multiple of 256, <= 4096)",
+                hidden);
+  if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
+      (logits && !aligned16(logits)) || !aligned16(workspace))
+    return fail(W4_ERR_ALIGNMENT, "w4_lm_head_argmax: pointers must be 16-byte aligned");
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  return launch_lm_head_argmax(h, norm_weight, eps, embed, vocab, hidden, logits, token, pos,
+                               workspace, pdl, (cudaStream_t)stream);
 }
 
 int w4_device_error(int device, int* code) {

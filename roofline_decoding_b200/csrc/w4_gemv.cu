@@ -36,6 +36,11 @@ namespace cg = cooperative_groups;
 
 namespace w4 {
 
+__device__ __forceinline__ float2 h2f2(uint32_t v, bool bf16) {
+  if (bf16) return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+
 struct GemvParams {
   const void* x;  // [M, K] fp16 / bf16
   void* y;        // [M, N] fp16 / bf16
@@ -45,7 +50,70 @@ struct GemvParams {
   int stages;            // ring depth
   int y_bf16;
   int* err;  // device error word
+  // fused operations (decode step); all zero for a plain GEMV
+  int pro;             // W4_PRO_*: transform applied to x while staging it
+  const void* pro_w;   // RMSNorm weight [K] (x's type)
+  float eps;           // RMSNorm epsilon
+  int epi;             // W4_EPI_*: transform applied to y before the store
+  const void* epi_src; // bias [N] or residual [M, N] (y's type; may alias y)
 };
+
+__device__ __forceinline__ float ld_f(const void* p, size_t i, bool bf16) {
+  const uint16_t v = static_cast<const uint16_t*>(p)[i];
+  return bf16 ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
+}
+__device__ __forceinline__ float round_to(float v, bool bf16) {
+  return bf16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  if (bf16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Applies the staging transform to 8 consecutive activations x[m, k..k+7]:
+//   RMSNorm: round(round(x * inv_rms[m]) * w[k])   (Qwen2/Llama RMSNorm: fp32
+//            normalisation, cast to the activation type, times the weight)
+//   SwiGLU : round(round(silu(g)) * u) with g = x[m, k], u = x[m, K + k] of a
+//            [M, 2K] gate|up row (silu in fp32, cast, product cast)
+template <bool kBF16>
+__device__ __forceinline__ uint4 stage_transform(const GemvParams& p, int m, int k, uint4 v,
+                                                 float inv_rms) {
+  if (p.pro == W4_PRO_RMSNORM) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.pro_w) + k));
+    const uint32_t* xi = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t* wi = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 o;
+    uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xf = h2f2(xi[i], kBF16), wf = h2f2(wi[i], kBF16);
+      oi[i] = pack2(round_to(xf.x * inv_rms, kBF16) * wf.x,
+                    round_to(xf.y * inv_rms, kBF16) * wf.y, kBF16);
+    }
+    return o;
+  }
+  if (p.pro == W4_PRO_SWIGLU) {
+    const uint16_t* row = static_cast<const uint16_t*>(p.x) + (size_t)m * 2 * p.K;
+    const uint4 uv = __ldcg(reinterpret_cast<const uint4*>(row + p.K + k));
+    const uint32_t* gi = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t* ui = reinterpret_cast<const uint32_t*>(&uv);
+    uint4 o;
+    uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 g = h2f2(gi[i], kBF16), u = h2f2(ui[i], kBF16);
+      const float sa = round_to(g.x / (1.0f + __expf(-g.x)), kBF16);
+      const float sb = round_to(g.y / (1.0f + __expf(-g.y)), kBF16);
+      oi[i] = pack2(sa * u.x, sb * u.y, kBF16);
+    }
+    return o;
+  }
+  return v;
+}
 
 template <int SW, int RG>
 struct TileShape {
@@ -67,15 +135,26 @@ __device__ __forceinline__ void report_error(int* err, int code) {
 }
 
 // Reorders the 8 activations of one packed row into the order the MMA
-// fragments consume them: (x0,x4) (x1,x5) (x2,x6) (x3,x7).
+// fragments consume them: (x0,x4) (x1,x5) (x2,x6) (x3,x7). For fp16 the odd
+// pairs meet the "1024 + 16q" form of unpack_nibbles and are pre-scaled by
+// 1/16 (exact for normal values; below 2^-10 the rounding error is under
+// 2^-25 absolute).
+template <bool kBF16>
 __device__ __forceinline__ uint4 permute_row(uint4 v) {
   uint4 o;
   o.x = __byte_perm(v.x, v.z, 0x5410);
   o.y = __byte_perm(v.x, v.z, 0x7632);
   o.z = __byte_perm(v.y, v.w, 0x5410);
   o.w = __byte_perm(v.y, v.w, 0x7632);
+  if constexpr (!kBF16) {
+    constexpr uint32_t kSixteenth = 0x2C002C00u;  // 1/16 | 1/16
+    constexpr uint32_t kZero = 0x80008000u;       // -0 | -0 (keeps x * 1/16 exact)
+    o.y = fma_f16x2(o.y, kSixteenth, kZero);
+    o.w = fma_f16x2(o.w, kSixteenth, kZero);
+  }
   return o;
 }
+
 
 template <bool kBF16, int MB, int SW, int RG>
 __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
@@ -93,7 +172,11 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
   uint8_t* s_w = smem;
   uint8_t* s_sc = s_w + S * T::kStageBytes;
   uint8_t* s_x = s_sc + S * T::kScaleSlot;
-  float* s_red = reinterpret_cast<float*>(s_x + M * plane);
+  // beta[m][group]: the constant the unpacked values carry, summed against the
+  // staged activations of each group (subtracted through the accumulator init)
+  float* s_beta = reinterpret_cast<float*>(s_x + M * plane);
+  float* s_inv = s_beta + ((M * p.groups_per_split + 3) & ~3);  // RMSNorm 1/rms per row
+  float* s_red = s_inv + 16;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_red + RG * M * T::kNT);
   uint64_t* empty = full + S;
 
@@ -117,9 +200,6 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     tma_prefetch_desc(&tm_s);
   }
   __syncthreads();
-  // Dependent grids may start their prologue (and their weight stream) now;
-  // they read our output only after their own grid-dependency wait.
-  grid_launch_dependents();
 
   // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
   // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
@@ -135,9 +215,10 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int issued = 0;
+      int slot = 0;
+      uint32_t phase = 0;  // phase of the current pass over the ring
       for (int j = 0; j < n_stages; ++j) {
-        const int slot = j % S;
-        if (j >= S && !mbar_wait(&empty[slot], ((j / S) - 1) & 1)) {
+        if (j >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
           report_error(p.err, kErrEmptyWait);
           break;
         }
@@ -149,7 +230,15 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
                       n0 + 32 * s, grp * 16);
         tma_load_2d(s_sc + slot * T::kScaleSlot, &tm_s, &full[slot], n0, grp);
         ++issued;
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1u;
+        }
       }
+      // All of this CTA's weight loads are in flight: dependent grids may be
+      // scheduled and start their own weight streams (they read this grid's
+      // output only after their grid-dependency wait).
+      grid_launch_dependents();
       // Do not leave while copies into this CTA's shared memory are in flight.
       for (int j = max(0, issued - S); j < issued; ++j)
         if (!mbar_wait(&full[j % S], (j / S) & 1)) report_error(p.err, kErrDrainWait);
@@ -160,31 +249,81 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     // x is produced by the previous kernel on the stream: wait for it.
     grid_dependency_wait();
     const uint16_t* xg = static_cast<const uint16_t*>(p.x);
+    // x row pitch: a SwiGLU prologue reads gate|up rows of 2K
+    const size_t x_pitch = (p.pro == W4_PRO_SWIGLU) ? 2 * (size_t)p.K : (size_t)p.K;
+    if (p.pro == W4_PRO_RMSNORM) {
+      // inv_rms[m] over the whole row (every CTA recomputes it: K <= 28672
+      // activations, served from L2), reduced in a fixed order
+      float* s_part = s_red;  // scratch: [kCW][M] partial sums (s_red is free until the epilogue)
+      for (int m = 0; m < M; ++m) {
+        float acc2 = 0.f;
+        for (int i = threadIdx.x; i < p.K / 8; i += nct) {
+          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xg + m * x_pitch + 8 * (size_t)i));
+          const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = h2f2(vi[e], kBF16);
+            acc2 = fmaf(f.x, f.x, acc2);
+            acc2 = fmaf(f.y, f.y, acc2);
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+        if (lane == 0) s_part[warp * M + m] = acc2;
+      }
+      consumer_bar_sync(nct);
+      if (threadIdx.x < M) {
+        float tot = 0.f;
+        for (int w = 0; w < T::kCW; ++w) tot += s_part[w * M + threadIdx.x];
+        s_inv[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
+      }
+      consumer_bar_sync(nct);
+    }
     // Batches of 4 independent 16-byte loads per thread, all in flight before
     // the first is consumed (one global round trip per batch, not per row).
+    // 16 consecutive threads hold the 16 rows of one group, so the group's
+    // correction beta is a 16-lane shuffle reduction (nct and rows_slice are
+    // multiples of 16, so a 16-lane group never straddles two groups).
     const int total = M * rows_slice;
-    for (int base = threadIdx.x; base < total; base += 4 * nct) {
+    // b0 is the same for every consumer thread, so all of them run the same
+    // trips and every shuffle below has its full warp
+    for (int b0 = 0; b0 < total; b0 += 4 * nct) {
       uint4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int idx = base + u * nct;
+        const int idx = b0 + u * nct + threadIdx.x;
         v[u] = make_uint4(0u, 0u, 0u, 0u);
         if (idx < total) {
           const int m = idx / rows_slice;
           const int krow = g0 * 16 + (idx - m * rows_slice);  // packed row = 8 activations
           if (krow < g1 * 16)
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(xg + (size_t)m * p.K +
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(xg + (size_t)m * x_pitch +
                                                           (size_t)krow * 8));
         }
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int idx = base + u * nct;
+        if (b0 + u * nct >= total) break;  // uniform over the consumer threads
+        const int idx = b0 + u * nct + threadIdx.x;
+        float lo = 0.f, hi = 0.f;
+        uint4 o = make_uint4(0u, 0u, 0u, 0u);
         if (idx < total) {
           const int m = idx / rows_slice;
           const int r = idx - m * rows_slice;
-          *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = permute_row(v[u]);
+          const int krow = g0 * 16 + r;
+          if (p.pro != W4_PRO_NONE && krow < g1 * 16)
+            v[u] = stage_transform<kBF16>(p, m, krow * 8, v[u], p.pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
+          o = permute_row<kBF16>(v[u]);
+          *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
+          const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
+          const float2 c = h2f2(o.z, kBF16), d = h2f2(o.w, kBF16);
+          lo = (a.x + a.y) + (c.x + c.y);
+          hi = (b.x + b.y) + (d.x + d.y);
         }
+        float bsum = kBF16 ? kBF16Offset * (lo + hi) : kF16LowOffset * lo + kF16HighOffset * hi;
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+        if (idx < total && (idx & 15) == 0) s_beta[idx >> 4] = bsum;
       }
     }
     consumer_bar_sync(nct);
@@ -193,44 +332,61 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     const int rg = warp / SW;
     const int g = lane >> 2;
     const int t = lane & 3;
-    const uint32_t s_w_u32 = smem_u32(s_w);
-    const uint32_t s_sc_u32 = smem_u32(s_sc);
-    const uint32_t s_x_u32 = smem_u32(s_x);
-    bool ok = true;
+    // Per-thread shared-memory offsets, fixed for the whole loop:
+    //   weights: rows rg*16 + 8*o + 2t + e of the strip box, 16-byte chunk g
+    //            stored at chunk g ^ (row & 7) by the 128B swizzle;
+    //   x:       lanes whose batch row g >= M read row M-1 instead, so every
+    //            lane loads unconditionally (their output columns are unused);
+    //   beta:    likewise clamped.
+    uint32_t w_off[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      w_off[e] = smem_u32(s_w) + strip * T::kStripBytes + (rg * 16 + 2 * t + e) * 128 +
+                 ((g ^ (2 * t + e)) << 4);
+    uint32_t x_off[MB];
+    const float* b_row[MB][2];
+#pragma unroll
+    for (int mb = 0; mb < MB; ++mb) {
+      x_off[mb] = smem_u32(s_x) + min(8 * mb + g, M - 1) * plane + 2 * t * 16;
+      b_row[mb][0] = s_beta + min(8 * mb + 2 * t, M - 1) * p.groups_per_split;
+      b_row[mb][1] = s_beta + min(8 * mb + 2 * t + 1, M - 1) * p.groups_per_split;
+    }
+    const uint32_t sc_off = smem_u32(s_sc) + (rg * T::kNT + 32 * strip + 4 * g) * 2;
 
-    for (int j = 0; j < n_stages && ok; ++j) {
-      const int slot = j % S;
-      if (!mbar_wait(&full[slot], (j / S) & 1)) {
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < n_stages; ++j) {
+      if (!mbar_wait(&full[slot], phase)) {
         report_error(p.err, kErrFullWait);
-        ok = false;
         break;
       }
-      const int grp = g0 + j * RG + rg;
-      if (grp < g1) {
+      const int gl = j * RG + rg;  // group inside the slice
+      if (gl < n_groups) {
+        // accumulators start at -beta of their batch row: the MMA sums then
+        // leave exactly sum_k (q - 8) x of this group
         float c[2][MB][4];
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+        for (int mb = 0; mb < MB; ++mb) {
+          const float nb0 = -b_row[mb][0][gl];
+          const float nb1 = -b_row[mb][1][gl];
 #pragma unroll
-          for (int b = 0; b < MB; ++b)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) c[a][b][i] = 0.f;
-
-        const uint32_t box = s_w_u32 + slot * T::kStageBytes + strip * T::kStripBytes;
+          for (int a = 0; a < 2; ++a) {
+            c[a][mb][0] = nb0;
+            c[a][mb][1] = nb1;
+            c[a][mb][2] = nb0;
+            c[a][mb][3] = nb1;
+          }
+        }
+        const uint32_t stage_base = slot * T::kStageBytes;
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int r = rg * 16 + 8 * o + 2 * t + e;  // row inside the strip box
-            // 128B swizzle: 16-byte chunk index XOR (row & 7).
-            const uint4 wv = lds128(box + r * 128 + ((g ^ (r & 7)) << 4));
-            const int xr = (grp - g0) * 16 + 8 * o + 2 * t + e;  // row inside the slice
+            const uint4 wv = lds128(w_off[e] + stage_base + o * 1024);
+            const uint32_t xrow = (gl * 16 + 8 * o + e) * 16;
             uint4 xb[MB];
 #pragma unroll
-            for (int mb = 0; mb < MB; ++mb) {
-              const int m = 8 * mb + g;
-              xb[mb] = (m < M) ? lds128(s_x_u32 + m * plane + xr * 16)
-                               : make_uint4(0u, 0u, 0u, 0u);
-            }
+            for (int mb = 0; mb < MB; ++mb) xb[mb] = lds128(x_off[mb] + xrow);
             uint32_t ha[4], hb[4];
             unpack_nibbles<kBF16>(wv.x, ha);  // column 4g
             unpack_nibbles<kBF16>(wv.y, hb);  // column 4g+1
@@ -249,9 +405,9 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
           }
         }
         // Scales of this group for columns (4g, 4g+1) and (4g+2, 4g+3).
-        const uint32_t sc_row = s_sc_u32 + slot * T::kScaleSlot + (rg * T::kNT + 32 * strip) * 2;
-        const uint32_t s01 = lds32(sc_row + (4 * g) * 2);
-        const uint32_t s23 = lds32(sc_row + (4 * g + 2) * 2);
+        const uint32_t sc = sc_off + slot * T::kScaleSlot;
+        const uint32_t s01 = lds32(sc);
+        const uint32_t s23 = lds32(sc + 4);
         const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&s01));
         const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
 #pragma unroll
@@ -268,6 +424,10 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == S) {
+        slot = 0;
+        phase ^= 1u;
+      }
     }
 
     // Per-warp partials into s_red[rg][m][col].
@@ -302,6 +462,13 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     const int m = idx / T::kNT;
     const int n = n0 + (idx - m * T::kNT);
     if (n < p.N) {
+      if (p.epi == W4_EPI_BIAS) {
+        v += ld_f(p.epi_src, n, p.y_bf16);  // one rounding, like a GEMM's bias epilogue
+      } else if (p.epi == W4_EPI_RESIDUAL) {
+        // out = round(residual + round(y)): the layer output is rounded before
+        // the residual add, as in the reference model's bf16 forward
+        v = ld_f(p.epi_src, (size_t)m * p.N + n, p.y_bf16) + round_to(v, p.y_bf16);
+      }
       if (p.y_bf16)
         static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v);
       else
@@ -371,7 +538,8 @@ size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& c) {
   const size_t stage = (size_t)c.strips * c.row_groups * 16 * 128;
   const size_t scale = ((size_t)c.row_groups * nt * 2 + 127) / 128 * 128;
   const size_t plane = (size_t)gps * 16 * 16 + 16;
-  return 1024 + c.stages * (stage + scale) + M * plane + c.row_groups * M * nt * 4 +
+  const size_t beta = (((size_t)M * gps + 3) & ~(size_t)3) * 4 + 16 * 4;
+  return 1024 + c.stages * (stage + scale) + M * plane + beta + c.row_groups * M * nt * 4 +
          2 * c.stages * sizeof(uint64_t);
 }
 
@@ -494,6 +662,11 @@ int launch_gemv(const GemvLaunch& L, cudaStream_t stream) {
   p.stages = c.stages;
   p.y_bf16 = L.y_bf16;
   p.err = di.err_word;
+  p.pro = L.ops.prologue;
+  p.pro_w = L.ops.norm_weight;
+  p.eps = L.ops.eps;
+  p.epi = L.ops.epilogue;
+  p.epi_src = L.ops.epi_src;
 
   const int threads = (c.strips * c.row_groups + 1) * 32;
   cudaLaunchConfig_t cfg = {};

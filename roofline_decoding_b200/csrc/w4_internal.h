@@ -39,6 +39,7 @@ struct GemvLaunch {
   int x_bf16, y_bf16;
   int M, K, N;
   w4_gemv_config cfg;
+  w4_fused_ops ops;  // zero for a plain GEMV
 };
 size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& cfg);
 int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const DeviceInfo& di);
@@ -46,6 +47,19 @@ int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const De
                        w4_gemv_config* out);
 int launch_gemv(const GemvLaunch& L, cudaStream_t stream);
 int gemv_init_device(const DeviceInfo& di);
+
+// Decode-step kernels (w4_decode.cu).
+int launch_decode_embed(const void* embed, int vocab, int hidden, const int64_t* prompt,
+                        const int64_t* prompt_len, int64_t* token, const int64_t* pos, void* h,
+                        int pdl, cudaStream_t stream);
+int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_t,
+                            const int64_t* pos, void* k_cache, void* v_cache, void* out, int heads,
+                            int kv_heads, int max_seq, int pdl, cudaStream_t stream);
+size_t lm_head_workspace_bytes();
+int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const void* embed,
+                          int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
+                          void* workspace, int pdl, cudaStream_t stream);
+int decode_init_device(const DeviceInfo& di);
 
 // Tensor-map encoder resolved from the driver at init.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

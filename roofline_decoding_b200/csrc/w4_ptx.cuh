@@ -13,6 +13,9 @@ namespace w4 {
 // A wait on an mbarrier gives up after this long and reports an error instead
 // of spinning forever (the kernels then drain their copies and return).
 constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+// Upper bound on one parked try_wait (the bounded wait re-checks its clock
+// between tries, so the 1 s limit still holds).
+constexpr uint32_t kSuspendHintNs = 20000;  // 20 us
 
 // Device-side error word; kernels set it when a bounded wait gives up.
 enum : int { kErrNone = 0, kErrFullWait = 1, kErrEmptyWait = 2, kErrDrainWait = 3 };
@@ -49,14 +52,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
+// One potentially blocking test of the phase. The suspend-time hint lets the
+// hardware park the thread until the phase completes (or the hint's time
+// passes) instead of returning at once, so waiting warps do not spin on the
+// issue slots the computing warps need.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -67,9 +74,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -131,37 +136,41 @@ __device__ __forceinline__ uint32_t fma_bf16x2(uint32_t a, uint32_t b, uint32_t 
   return d;
 }
 
-// Unpacks the 8 nibbles of one packed word into four 16-bit pairs holding the
-// exact values q - 8:  h[0] = (q0, q4), h[1] = (q1, q5), h[2] = (q2, q6),
-// h[3] = (q3, q7)  (first element in the low half).
-//
-// The nibble is OR-ed into the mantissa of a constant whose mantissa unit is
-// one (fp16 1024.0 = 0x6400, bf16 128.0 = 0x4300), which turns the 4-bit
-// integer into a float in a single LOP3; one FMA removes the constant and the
-// zero point. All values involved are small integers, so every step is exact.
+// Unpacks the 8 nibbles of one packed word into four 16-bit pairs of
+// small exact integers, with one LOP3 per pair: the nibble is OR-ed into the
+// mantissa of a constant whose mantissa unit is one, turning it into a float
+// without a conversion instruction.
+//   fp16: h[0] = (1024+q0, 1024+q4)        h[1] = (1024+16q1, 1024+16q5)
+//         h[2] = (1024+q2, 1024+q6)        h[3] = (1024+16q3, 1024+16q7)
+//   bf16: h[i] = (128+q_i, 128+q_{i+4})    (the 16q form does not fit bf16)
+// (first element in the low half). The constant and the zero point are not
+// removed here: the GEMV folds them into one per-(group, row) correction, and
+// the fp16 "16q" slots meet activations pre-scaled by 1/16.
 template <bool kBF16>
 __device__ __forceinline__ void unpack_nibbles(uint32_t w, uint32_t (&h)[4]) {
   if constexpr (!kBF16) {
-    constexpr uint32_t kMagic = 0x64006400u;   // 1024 | 1024
-    constexpr uint32_t kOne = 0x3C003C00u;     // 1.0
-    constexpr uint32_t kSub = 0xE408E408u;     // -1032 = -(1024 + 8)
-    constexpr uint32_t kSixteenth = 0x2C002C00u;  // 1/16
-    constexpr uint32_t kSub16 = 0xD480D480u;   // -72 = -(1024/16 + 8)
+    constexpr uint32_t kMagic = 0x64006400u;  // 1024 | 1024
     const uint32_t w8 = w >> 8;
-    h[0] = fma_f16x2(lop3_and_or(w, 0x000F000Fu, kMagic), kOne, kSub);
-    h[1] = fma_f16x2(lop3_and_or(w, 0x00F000F0u, kMagic), kSixteenth, kSub16);
-    h[2] = fma_f16x2(lop3_and_or(w8, 0x000F000Fu, kMagic), kOne, kSub);
-    h[3] = fma_f16x2(lop3_and_or(w8, 0x00F000F0u, kMagic), kSixteenth, kSub16);
+    h[0] = lop3_and_or(w, 0x000F000Fu, kMagic);
+    h[1] = lop3_and_or(w, 0x00F000F0u, kMagic);
+    h[2] = lop3_and_or(w8, 0x000F000Fu, kMagic);
+    h[3] = lop3_and_or(w8, 0x00F000F0u, kMagic);
   } else {
     constexpr uint32_t kMagic = 0x43004300u;  // 128 | 128
-    constexpr uint32_t kOne = 0x3F803F80u;    // 1.0
-    constexpr uint32_t kSub = 0xC308C308u;    // -136 = -(128 + 8)
-    h[0] = fma_bf16x2(lop3_and_or(w, 0x000F000Fu, kMagic), kOne, kSub);
-    h[1] = fma_bf16x2(lop3_and_or(w >> 4, 0x000F000Fu, kMagic), kOne, kSub);
-    h[2] = fma_bf16x2(lop3_and_or(w >> 8, 0x000F000Fu, kMagic), kOne, kSub);
-    h[3] = fma_bf16x2(lop3_and_or(w >> 12, 0x000F000Fu, kMagic), kOne, kSub);
+    h[0] = lop3_and_or(w, 0x000F000Fu, kMagic);
+    h[1] = lop3_and_or(w >> 4, 0x000F000Fu, kMagic);
+    h[2] = lop3_and_or(w >> 8, 0x000F000Fu, kMagic);
+    h[3] = lop3_and_or(w >> 12, 0x000F000Fu, kMagic);
   }
 }
+
+// Per-element offsets the unpacked values carry, for the correction term:
+//   fp16 low-nibble slots (h[0], h[2]) hold (q - 8) + 1032 against x,
+//   fp16 high-nibble slots (h[1], h[3]) hold 16 * ((q - 8) + 72) against x/16,
+//   bf16 slots hold (q - 8) + 136 against x.
+constexpr float kF16LowOffset = 1032.0f;
+constexpr float kF16HighOffset = 72.0f * 16.0f;  // applied to the staged x/16
+constexpr float kBF16Offset = 136.0f;
 
 // D += A(16x16, row) * B(16x8, col), fp32 accumulate.
 template <bool kBF16>

@@ -232,6 +232,28 @@ def w4_matmul(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
     return y[0] if squeeze else y
 
 
+def fused_launch(x2: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
+                 y: torch.Tensor, cfg: GemvConfig, prologue: int = 0,
+                 norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                 epilogue: int = 0, epi_src: torch.Tensor | None = None) -> None:
+    """One fused GEMV launch (w4_gemv_fused): prologue on x, epilogue on y.
+
+    prologue: _lib.W4_PRO_RMSNORM (x <- rmsnorm(x) * norm_weight) or
+    _lib.W4_PRO_SWIGLU (x is [M, 2K] gate|up, x <- silu(gate) * up);
+    epilogue: _lib.W4_EPI_BIAS (y += epi_src[n]) or _lib.W4_EPI_RESIDUAL
+    (y <- epi_src + round(y); epi_src may be y itself).
+    """
+    M = x2.shape[0]
+    K = packed.shape[0] * 8
+    N = packed.shape[1]
+    ops = _lib.FusedOps(int(prologue), norm_weight.data_ptr() if norm_weight is not None else None,
+                        float(eps), int(epilogue),
+                        epi_src.data_ptr() if epi_src is not None else None)
+    check(_lib.load().w4_gemv_fused(x2.data_ptr(), _DTYPE_CODE[x2.dtype], packed.data_ptr(),
+                                    scales.data_ptr(), y.data_ptr(), _DTYPE_CODE[y.dtype], M, K,
+                                    N, ops, cfg, _stream_ptr(x2.device)), "w4_gemv_fused")
+
+
 def gemv_v2(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
             out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Fused GEMV, x [K] -> y [N] fp16 (roofline/kernels.py:131-145).

@@ -353,3 +353,69 @@ def test_tuner_picks_a_working_config():
     assert len(table) >= 4
     assert table[0][1] == best.as_tuple()
     check_gemv(1536, 1536, config=best)
+
+
+# ---------------------------------------------------------------- fused GEMV ops
+
+def _bf16_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV).to(torch.bfloat16)
+
+
+def _fused_case(Kd, N, M, seed):
+    p, s = pack_dev(gen(Kd, N, seed=seed))
+    w_ex = torch.from_numpy(o.dequantize_f32(p.cpu().numpy(), s.cpu().numpy())).to(DEV)
+    return p, s, w_ex.double()
+
+
+@pytest.mark.parametrize("M", [1, 3])
+def test_fused_rmsnorm_prologue_and_bias(M):
+    """x <- round(round(x * rsqrt(mean(x^2) + eps)) * w); y <- round(x @ W + b)."""
+    from roofline_decoding_b200 import _lib
+
+    Kd, N = 1536, 2048
+    p, s, w_ex = _fused_case(Kd, N, M, 21)
+    rng = np.random.default_rng(3)
+    x = _bf16_dev(rng.standard_normal((M, Kd)) * 2.0)
+    nw = _bf16_dev(1.0 + 0.05 * rng.standard_normal(Kd))
+    b = _bf16_dev(0.1 * rng.standard_normal(N))
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None)
+    K.fused_launch(x, p, s, y, cfg, _lib.W4_PRO_RMSNORM, nw, 1e-6, _lib.W4_EPI_BIAS, b)
+    xf = x.float()
+    xn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    xs = (nw * xn).double()  # bf16 * bf16 -> bf16, as the reference model's RMSNorm
+    want = (xs @ w_ex + b.double())
+    torch.testing.assert_close(y.double(), want, rtol=2 ** -8 * 1.01, atol=1e-3)
+
+
+@pytest.mark.parametrize("M", [1, 2])
+def test_fused_swiglu_prologue_and_residual(M):
+    """x <- round(round(silu(g)) * u) of a gate|up row; y <- round(r + round(x @ W))."""
+    from roofline_decoding_b200 import _lib
+
+    Kd, N = 8960, 1536
+    p, s, w_ex = _fused_case(Kd, N, M, 22)
+    rng = np.random.default_rng(4)
+    gu = _bf16_dev(rng.standard_normal((M, 2 * Kd)))
+    res = _bf16_dev(rng.standard_normal((M, N)))
+    y = res.clone()  # in place: residual aliases the output
+    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None)
+    K.fused_launch(gu, p, s, y, cfg, _lib.W4_PRO_SWIGLU, epilogue=_lib.W4_EPI_RESIDUAL, epi_src=y)
+    g, u = gu[:, :Kd], gu[:, Kd:]
+    act = (torch.nn.functional.silu(g) * u).double()  # bf16 silu, bf16 product
+    lin = (act @ w_ex).to(torch.bfloat16)
+    want = (res.double() + lin.double())
+    torch.testing.assert_close(y.double(), want, rtol=2 ** -7, atol=2e-2)
+
+
+def test_fused_ops_reject_bad_arguments():
+    from roofline_decoding_b200 import _lib
+
+    p, s, _ = _fused_case(256, 64, 1, 1)
+    x = torch.randn(1, 256, device=DEV, dtype=torch.bfloat16)
+    y = torch.empty(1, 64, device=DEV, dtype=torch.bfloat16)
+    cfg = K.default_config(1, 256, 64)
+    with pytest.raises(ValueError):  # RMSNorm without a weight
+        K.fused_launch(x, p, s, y, cfg, _lib.W4_PRO_RMSNORM)
+    with pytest.raises(ValueError):  # residual without a source
+        K.fused_launch(x, p, s, y, cfg, epilogue=_lib.W4_EPI_RESIDUAL)
