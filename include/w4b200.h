@@ -168,6 +168,26 @@ int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps,
                       int64_t* token, int64_t* pos, void* workspace,
                       size_t workspace_bytes, int pdl, void* stream);
 
+/* w4_lm_head_argmax for hosts that cannot allocate device memory. There is
+ * no counterpart of this entry point in the reference.
+ *
+ * Some callers of this library may not allocate: a C or C++ decode loop in
+ * a process whose device memory belongs to another runtime's pool, or a
+ * plugin that must not call an allocator once it is serving. This variant
+ * needs no workspace: the argmax state lives in a 256-byte array inside the
+ * library's module, present on every GPU that loads the library until the
+ * process exits. It allocates and frees nothing. Its first call on a device
+ * looks up that array's address and clears it on the given stream, so make
+ * that first call before any stream capture. All calls on a device share the
+ * one array: calls that overlap on the GPU race. vocab may not exceed
+ * W4B200_STATIC_SCRATCH_MAX_VOCAB (the state keeps a 32-bit row index);
+ * other arguments as w4_lm_head_argmax. */
+#define W4B200_STATIC_SCRATCH_MAX_VOCAB 0x7fffffff
+int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
+                             const void* embed, int vocab, int hidden,
+                             void* logits, int64_t* token, int64_t* pos,
+                             int pdl, void* stream);
+
 /* Reads and clears the device-side error word that kernels set when a
  * bounded wait gives up (0 = no error). Synchronises the device. */
 int w4_device_error(int device, int* code);

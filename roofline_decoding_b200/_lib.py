@@ -91,6 +91,9 @@ SIGNATURES = {
     "w4_lm_head_argmax": (_c_int, [_c_void_p, _c_void_p, ctypes.c_float, _c_void_p, _c_int,
                                    _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                    _c_size_t, _c_int, _c_void_p]),
+    "w4_lm_head_argmax_static": (_c_int, [_c_void_p, _c_void_p, ctypes.c_float, _c_void_p,
+                                          _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
+                                          _c_void_p]),
     "w4_device_error": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
 }
 

@@ -301,6 +301,29 @@ int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps, const v
                                workspace, pdl, (cudaStream_t)stream);
 }
 
+int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
+                             const void* embed, int vocab, int hidden, void* logits,
+                             int64_t* token, int64_t* pos, int pdl, void* stream) {
+  if (!h || !norm_weight || !embed || !token || !pos)
+    return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax_static: null pointer");
+  if (vocab <= 0 || (long long)vocab > (long long)W4B200_STATIC_SCRATCH_MAX_VOCAB)
+    return fail(W4_ERR_INVALID_ARG,
+                "w4_lm_head_argmax_static: vocab=%d outside 1..%lld (the static argmax state "
+                "keeps a 32-bit row index)",
+                vocab, (long long)W4B200_STATIC_SCRATCH_MAX_VOCAB);
+  if (hidden % 256 != 0 || hidden < 256 || hidden > 4096)
+    return fail(W4_ERR_UNSUPPORTED,
+                "w4_lm_head_argmax_static: hidden=%d (multiple of 256, <= 4096)", hidden);
+  if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
+      (logits && !aligned16(logits)))
+    return fail(W4_ERR_ALIGNMENT, "w4_lm_head_argmax_static: pointers must be 16-byte aligned");
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  return lm_head_argmax_static(h, norm_weight, eps, embed, vocab, hidden, logits, token, pos,
+                               pdl, (cudaStream_t)stream);
+}
+
 int w4_device_error(int device, int* code) {
   if (!code) return fail(W4_ERR_INVALID_ARG, "w4_device_error: null out");
   int st = w4_init(device);

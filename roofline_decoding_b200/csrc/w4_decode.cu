@@ -16,6 +16,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <mutex>
 
 namespace cg = cooperative_groups;
 
@@ -458,6 +459,52 @@ int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const vo
     default: return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden %d not in {256, 512, 1024, 1536, 2048, 4096}", hidden);
   }
   return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_lm_head_argmax launch");
+}
+
+// ------------------------------------------------------------------ allocation-free lm_head
+//
+// Some hosts cannot hand this library device memory: a C or C++ decode loop
+// embedded in a process whose device memory is owned by someone else's pool,
+// or a plugin that is not allowed to call an allocator once serving has
+// started. For them the argmax state of the lm_head kernel lives in a fixed
+// array that the module itself provides. Every call on a device shares that
+// one array, so calls that overlap on the GPU race with each other.
+constexpr size_t kStaticScratchBytes = 256;
+static_assert(sizeof(LmHeadWorkspace) <= kStaticScratchBytes,
+              "the lm_head argmax state must fit the static scratch");
+static __device__ __align__(256) unsigned char g_lm_head_scratch[kStaticScratchBytes];
+
+namespace {
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch[64] = {};  // device address of g_lm_head_scratch, per device
+}  // namespace
+
+int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const void* embed,
+                          int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
+                          int pdl, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(W4_ERR_UNSUPPORTED, "device %d", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (!g_static_scratch[dev]) {
+      // In host code g_lm_head_scratch only names the array; the kernel needs
+      // its address on this device.
+      e = cudaGetSymbolAddress(&scratch, g_lm_head_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(lm_head scratch)");
+      // The array is zero when the module loads and every finished call
+      // leaves it zero; clearing it here also recovers from a call that was
+      // cut short.
+      e = cudaMemsetAsync(scratch, 0, sizeof(LmHeadWorkspace), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "clearing the lm_head scratch");
+      g_static_scratch[dev] = scratch;
+    }
+    scratch = g_static_scratch[dev];
+  }
+  return launch_lm_head_argmax(h, norm_w, eps, embed, vocab, hidden, logits, token, pos,
+                               scratch, pdl, stream);
 }
 
 int decode_init_device(const DeviceInfo& di) {

@@ -59,6 +59,9 @@ size_t lm_head_workspace_bytes();
 int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const void* embed,
                           int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
                           void* workspace, int pdl, cudaStream_t stream);
+int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const void* embed,
+                          int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
+                          int pdl, cudaStream_t stream);
 int decode_init_device(const DeviceInfo& di);
 
 // Tensor-map encoder resolved from the driver at init.
