@@ -20,10 +20,11 @@ weights from HBM (the pool exceeds 3x L2).
             full unsharded GEMV) of all ranks / max-over-ranks time, GB/s.
             Region A: one CUDA graph per rotation slot with the GEMVs chained
             by programmatic dependent launch, replayed back to back.
-  per_case / roofline: region B, the same launches without PDL and with an
-            event after every kernel; roofline = the GEMV with the largest
-            mean kernel time, bytes per launch / its mean duration, against
-            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  per_case / roofline: region B, for each GEMV a CUDA graph of PDL-chained
+            launches of that GEMV alone on weight copies exceeding 3x L2
+            (events around the chain, time per launch); roofline = the GEMV
+            with the largest launch time, bytes per launch / that time,
+            against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
   e2e     : the public API (w4_matmul) with x copied from pinned host memory
             and y copied back for every GEMV, one host sync per step.
   cpu_baseline: the reference's dequantise-then-matmul path restated in C
@@ -351,11 +352,8 @@ def run_gemv_workload(args, rank, world, local):
     graphs_pdl = [capture(si, True, None) for si in range(slots)]
     graphs_gemv = [capture(si, True, None, gather=False) for si in range(slots)] \
         if sharded else []
-    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(n_launch + 1)]
-           for _ in range(slots)]
-    graphs_ev = [capture(si, False, evs[si], gather=False) for si in range(slots)]
     with torch.cuda.stream(stream):  # upload every graph before any timing
-        for g in graphs_pdl + graphs_ev + graphs_gemv:
+        for g in graphs_pdl + graphs_gemv:
             g.replay()
     torch.cuda.synchronize()
 
@@ -380,22 +378,11 @@ def run_gemv_workload(args, rank, world, local):
     with ClockSampler(local) as clocks:
         ms_a = timed(graphs_pdl, args.steps, args.warmup)
         ms_gemv = timed(graphs_gemv, args.steps, args.warmup) if sharded else 0.0
-        # region B: per-kernel event times, one pass over the slots at a time
-        per_kernel = [[] for _ in range(n_launch)]
-        done = 0
-        with torch.cuda.stream(stream):
-            while done < args.steps:
-                n = min(slots, args.steps - done)
-                for si in range(n):
-                    graphs_ev[si].replay()
-                stream.synchronize()
-                for si in range(n):
-                    for k in range(n_launch):
-                        per_kernel[k].append(evs[si][k].elapsed_time(evs[si][k + 1]))
-                done += n
-        torch.cuda.synchronize()
+        # region B: per GEMV, a chain of dependent launches of that GEMV alone
+        per_kernel = [chain_time(torch, Kn, xs[k], ys[k], pool[0][k], cfgs[k], l2, stream)
+                      for k in range(n_launch)]
     elapsed_ms, ms_gemv = max_over_ranks([ms_a, ms_gemv], world)
-    mean_k = max_over_ranks([statistics.mean(v) for v in per_kernel], world)
+    mean_k = max_over_ranks(per_kernel, world)  # ms per launch
 
     full_bytes = [gemv_bytes(M, K, N) for M, K, N, dt in cases]
     local_bytes = [gemv_bytes(M, K, n) for (M, K, N, dt), n in zip(cases, n_loc)]
@@ -439,8 +426,9 @@ def run_gemv_workload(args, rank, world, local):
                               f"{l2 / 2**20:.0f} MiB)"),
                        "timing": "value: CUDA graph per rotation slot, GEMVs chained with "
                                  "programmatic dependent launch, events around the steps, "
-                                 "max over ranks; per_case/roofline: the same launches "
-                                 "without PDL, an event after every kernel"},
+                                 "max over ranks; per_case/roofline: per GEMV, a CUDA graph "
+                                 "of PDL-chained launches of that GEMV alone, each on its own "
+                                 "weight copy (copies exceed 3x L2), events around the chain"},
             "gpu_launches": n_launch * args.steps,
             "roofline": {"bound": "hbm",
                          "kernel": f"w4_gemv_kernel M={dM} K={dK} N={n_loc[dom]} act={ddt}",
@@ -448,7 +436,9 @@ def run_gemv_workload(args, rank, world, local):
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": None, "bytes_per_launch": local_bytes[dom],
                          "mean_launch_us": round(dom_us, 3),
-                         "sum_isolated_kernel_us_per_step": round(sum(mean_k) * 1e3, 2),
+                         "timing": "mean launch of a PDL chain of this GEMV over "
+                                   "weight copies exceeding 3x L2 (region B)",
+                         "sum_chained_kernel_us_per_step": round(sum(mean_k) * 1e3, 2),
                          "pdl_chained_us_per_step": round(elapsed_ms * 1e3 / args.steps, 2)},
             "per_case": per_case,
             "measured_copy_gbs": round(copy_gbs, 1),
@@ -460,7 +450,40 @@ def run_gemv_workload(args, rank, world, local):
             line["gemv_only_ms_per_step"] = round(ms_gemv / args.steps, 4)
             line["gather_ms_per_step"] = round((elapsed_ms - ms_gemv) / args.steps, 4)
         print(json.dumps(line), flush=True)
-    del graphs_pdl, graphs_ev, graphs_gemv  # graphs holding NCCL calls go first
+    del graphs_pdl, graphs_gemv  # graphs holding NCCL calls go first
+
+
+def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
+    """ms per launch of one GEMV in a graph of dependent (PDL) launches.
+
+    Every launch reads its own copy of the packed weights and the copies
+    exceed 3x L2, so each launch streams from HBM as in a decode step; the
+    chain is long enough that event resolution does not matter.
+    """
+    from roofline_decoding_b200._lib import GemvConfig
+
+    packed, scales = weights
+    wbytes = packed.numel() * 4 + scales.numel() * 2
+    n = int(min(2048, max(8, -(-3 * l2 // wbytes))))
+    copies = [(packed.clone(), scales.clone()) for _ in range(n)]
+    c = GemvConfig(cfg.strips, cfg.row_groups, cfg.stages, cfg.split, 1)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for pk, sc in copies:
+                Kn.w4_matmul(x, pk, sc, out=y, config=c)
+        g.replay()  # upload
+        best = float("inf")
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            b.synchronize()
+            best = min(best, a.elapsed_time(b) / n)
+    del g, copies
+    return best
 
 
 def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered, n_loc):
@@ -536,7 +559,9 @@ def run_decode(args, rank, world, local):
         torch.cuda.synchronize()
     ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
     tok_s = world * args.steps / (ms / 1e3)
-    step_bytes = model.bytes_per_step()  # the attention reads the whole static cache
+    # the attention reads positions 0..pos: bytes at the mean position of the timed steps
+    mean_seq = prompt_len + args.warmup + (args.steps + 1) // 2
+    step_bytes = model.bytes_per_step(seq_len=mean_seq)
     achieved = step_bytes * (args.steps / (ms / 1e3)) / 1e9
 
     # e2e: a host-driven loop that reads every token (like .item() per token)
@@ -571,11 +596,12 @@ def run_decode(args, rank, world, local):
                                "int4 linears, tied bf16 lm_head 1536x151936, static KV 2048",
                    "prompt": prompt_len, "global_batch": world,
                    "parallelism": f"replicas{world}"},
-        "gpu_launches": None,
+        "gpu_launches": (2 + 5 * model.cfg.layers) * args.steps,
         "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None, "bytes_per_step": step_bytes,
+                     "kv_positions_read": mean_seq,
                      "ceiling_tok_s": round(peak * 1e9 / step_bytes, 1)},
         "e2e": {"value": round(world * args.steps / (ms2 / 1e3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,

@@ -161,7 +161,7 @@ size_t w4_lm_head_workspace_bytes(void);
 /* w4_lm_head_argmax: x = rmsnorm(h) * norm_weight, logits[v] = embed[v, :]
  * . x (bf16, the tied embedding as lm_head), token <- argmax (first index
  * among equal bf16 logits, like torch.argmax), pos <- pos + 1. logits may be
- * NULL. The workspace (w4_lm_head_workspace_bytes, zeroed before the first
+ * NULL. hidden is one of 256, 512, 1024, 1536, 2048. The workspace (w4_lm_head_workspace_bytes, zeroed before the first
  * call) carries the cross-CTA argmax and is left zeroed again. */
 int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps,
                       const void* embed, int vocab, int hidden, void* logits,

@@ -288,8 +288,8 @@ int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps, const v
   if (workspace_bytes < lm_head_workspace_bytes())
     return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax: workspace of %zu bytes < %zu",
                 workspace_bytes, lm_head_workspace_bytes());
-  if (vocab <= 0 || hidden % 256 != 0 || hidden < 256 || hidden > 4096)
-    return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden=%d (multiple of 256, <= 4096)",
+  if (vocab <= 0 || hidden % 256 != 0 || hidden < 256 || hidden > 2048)
+    return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden=%d (multiple of 256, <= 2048)",
                 hidden);
   if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
       (logits && !aligned16(logits)) || !aligned16(workspace))
@@ -311,9 +311,9 @@ int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
                 "w4_lm_head_argmax_static: vocab=%d outside 1..%lld (the static argmax state "
                 "keeps a 32-bit row index)",
                 vocab, (long long)W4B200_STATIC_SCRATCH_MAX_VOCAB);
-  if (hidden % 256 != 0 || hidden < 256 || hidden > 4096)
+  if (hidden % 256 != 0 || hidden < 256 || hidden > 2048)
     return fail(W4_ERR_UNSUPPORTED,
-                "w4_lm_head_argmax_static: hidden=%d (multiple of 256, <= 4096)", hidden);
+                "w4_lm_head_argmax_static: hidden=%d (multiple of 256, <= 2048)", hidden);
   if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
       (logits && !aligned16(logits)))
     return fail(W4_ERR_ALIGNMENT, "w4_lm_head_argmax_static: pointers must be 16-byte aligned");

@@ -102,149 +102,208 @@ __device__ __forceinline__ float rope_dim(const uint16_t* head, int d, float c, 
   return rbf(rbf(x * c) + rbf(rot * s));
 }
 
-// Shared memory (floats): q[G][128], kn[128], vn[128], scores[chunk][G],
-// warp partials wm[4][G], wl[4][G], wo[4][G][128], cluster partials
-// pm[G], pl[G], po[G][128].
+// Positions per shared-memory tile of the split's K/V range.
+constexpr int kAttnTile = 64;
+constexpr int kKPitch = kHeadDim + 2;  // bf16 per K row: +1 word, conflict-free column reads
+constexpr int kQPitch = kHeadDim + 4;  // floats per q row: rows land on different banks
+
+// Shared memory layout (attn_smem_bytes gives its size):
+//   raw   bf16 [(G + 2) * 128]           this token's q (G heads), k, v
+//   q_s   f32  [G][kQPitch]              q after RoPE
+//   kn_s  f32  [128], vn_s f32 [128]     this token's k (after RoPE) and v
+//   kt_s  bf16 [kAttnTile][kKPitch]      K rows of the current tile
+//   vt_s  bf16 [kAttnTile][128]          V rows of the current tile
+//   sc_s  f32  [kAttnTile][G]            scores, then probabilities, of the tile
+//   hm_s, hl_s, ha_s  f32 [G]            running max, sum and rescale factor
+//   pm_s, pl_s f32 [G], po_s f32 [G][128]  this split's partial result
+struct AttnSmem {
+  uint16_t* raw;
+  float* q_s;
+  float* kn_s;
+  float* vn_s;
+  uint16_t* kt_s;
+  uint16_t* vt_s;
+  float* sc_s;
+  float* hm_s;
+  float* hl_s;
+  float* ha_s;
+  float* pm_s;
+  float* pl_s;
+  float* po_s;
+};
+
+__host__ __device__ inline size_t attn_raw_bytes(int G) {
+  return ((size_t)(G + 2) * kHeadDim * 2 + 15) / 16 * 16;
+}
+
+__device__ __forceinline__ AttnSmem attn_layout(unsigned char* base, int G) {
+  AttnSmem m;
+  m.raw = reinterpret_cast<uint16_t*>(base);
+  m.q_s = reinterpret_cast<float*>(base + attn_raw_bytes(G));
+  m.kn_s = m.q_s + G * kQPitch;
+  m.vn_s = m.kn_s + kHeadDim;
+  m.kt_s = reinterpret_cast<uint16_t*>(m.vn_s + kHeadDim);
+  m.vt_s = m.kt_s + kAttnTile * kKPitch;
+  m.sc_s = reinterpret_cast<float*>(m.vt_s + kAttnTile * kHeadDim);
+  m.hm_s = m.sc_s + kAttnTile * G;
+  m.hl_s = m.hm_s + G;
+  m.ha_s = m.hl_s + G;
+  m.pm_s = m.ha_s + G;
+  m.pl_s = m.pm_s + G;
+  m.po_s = m.pl_s + G;
+  return m;
+}
+
+static size_t attn_smem_bytes(int G) {
+  const size_t f32 = (size_t)G * kQPitch + 2 * kHeadDim;
+  const size_t tiles = (size_t)kAttnTile * kKPitch * 2 + (size_t)kAttnTile * kHeadDim * 2;
+  const size_t rest = (size_t)kAttnTile * G + 5 * (size_t)G + (size_t)G * kHeadDim;
+  return attn_raw_bytes(G) + f32 * 4 + tiles + rest * 4 + 16;
+}
+
+// Loads cache rows [t0, t1) into the tile (none of them the new position).
+__device__ __forceinline__ void load_tile(const AttnSmem& sm, const uint16_t* kc,
+                                          const uint16_t* vc, int t0, int t1, int tid) {
+  const int n = t1 - t0;
+  for (int i = tid; i < n * 16; i += kAttnThreads) {  // 16 uint4 per row for K and V each
+    const int r = i >> 4, c = i & 15;
+    const uint4 kv = __ldcg(reinterpret_cast<const uint4*>(kc + (size_t)(t0 + r) * kHeadDim) + c);
+    const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(vc + (size_t)(t0 + r) * kHeadDim) + c);
+    // K rows have an odd word pitch: store them word by word
+    uint32_t* kd = reinterpret_cast<uint32_t*>(sm.kt_s + r * kKPitch) + 4 * c;
+    kd[0] = kv.x;
+    kd[1] = kv.y;
+    kd[2] = kv.z;
+    kd[3] = kv.w;
+    *(reinterpret_cast<uint4*>(sm.vt_s + r * kHeadDim) + c) = vv;
+  }
+}
+
+// Flash-decoding over this split's positions in tiles of kAttnTile: scores
+// one thread per (position, head) from shared memory, online softmax per head,
+// P.V one thread per dimension; the splits merge over DSMEM in rank order.
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) unsigned char smem_attn[];
   const int G = p.group;
   const int kvh = blockIdx.x;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const AttnSmem sm = attn_layout(smem_attn, G);
 
-  grid_dependency_wait();  // qkv comes from the previous kernel
-  // a position outside the cache is clamped (wrong output, never a wild store)
+  // The position and the cached rows below it were written by earlier steps:
+  // load the first tile before waiting for this step's q/k/v.
   const int64_t raw_pos = *p.pos;
+  // a position outside the cache is clamped (wrong output, never a wild store)
   const int pos = raw_pos < 0 ? 0 : (raw_pos >= p.max_seq ? p.max_seq - 1 : (int)raw_pos);
   const int P = pos + 1;
   const int chunk = (P + kAttnSplits - 1) / kAttnSplits;
-  const int max_chunk = (p.max_seq + kAttnSplits - 1) / kAttnSplits;
-  const int j0 = rank * chunk, j1 = min(P, j0 + chunk);
+  const int j0 = min(P, rank * chunk), j1 = min(P, j0 + chunk);
+  const uint16_t* kc = p.k_cache + (size_t)kvh * p.max_seq * kHeadDim;
+  const uint16_t* vc = p.v_cache + (size_t)kvh * p.max_seq * kHeadDim;
+  load_tile(sm, kc, vc, j0, min(min(j1, j0 + kAttnTile), pos), tid);
+  const float c = bf(p.cos_t[(size_t)pos * kHeadDim + tid]);
+  const float s = bf(p.sin_t[(size_t)pos * kHeadDim + tid]);
+  if (tid < G) {
+    sm.hm_s[tid] = -INFINITY;
+    sm.hl_s[tid] = 0.f;
+  }
 
-  float* q_s = sm;                       // [G][128]
-  float* kn_s = q_s + G * kHeadDim;      // [128]
-  float* vn_s = kn_s + kHeadDim;         // [128]
-  float* sc_s = vn_s + kHeadDim;         // [max_chunk][G]
-  float* wm_s = sc_s + max_chunk * G;    // [4][G]
-  float* wl_s = wm_s + 4 * G;            // [4][G]
-  float* wo_s = wl_s + 4 * G;            // [4][G][128]
-  float* pm_s = wo_s + 4 * G * kHeadDim; // [G]
-  float* pl_s = pm_s + G;                // [G]
-  float* po_s = pl_s + G;                // [G][128]
-
-  // RoPE on the group's q heads and on k; v as is.
-  {
-    const float c = bf(p.cos_t[(size_t)pos * kHeadDim + tid]);
-    const float s = bf(p.sin_t[(size_t)pos * kHeadDim + tid]);
-    for (int h = 0; h < G; ++h)
-      q_s[h * kHeadDim + tid] = rope_dim(p.qkv + (size_t)(kvh * G + h) * kHeadDim, tid, c, s);
-    const uint16_t* kh = p.qkv + (size_t)p.heads * kHeadDim + (size_t)kvh * kHeadDim;
-    const uint16_t* vh = p.qkv + (size_t)(p.heads + p.kv_heads) * kHeadDim + (size_t)kvh * kHeadDim;
-    const float kr = rope_dim(kh, tid, c, s);
-    const float vv = bf(vh[tid]);
-    kn_s[tid] = kr;
-    vn_s[tid] = vv;
-    if (pos >= j0 && pos < j1) {  // this CTA owns the new position: store it
-      const size_t at = ((size_t)kvh * p.max_seq + pos) * kHeadDim + tid;
-      p.k_cache[at] = to_bf(kr);
-      p.v_cache[at] = to_bf(vv);
+  grid_dependency_wait();  // qkv comes from the previous kernel
+  {  // this group's q heads, k and v in one vectorised pass
+    const uint4* q = reinterpret_cast<const uint4*>(p.qkv + (size_t)kvh * G * kHeadDim);
+    const uint4* k = reinterpret_cast<const uint4*>(p.qkv + (size_t)(p.heads + kvh) * kHeadDim);
+    const uint4* v =
+        reinterpret_cast<const uint4*>(p.qkv + (size_t)(p.heads + p.kv_heads + kvh) * kHeadDim);
+    uint4* dst = reinterpret_cast<uint4*>(sm.raw);
+    for (int i = tid; i < (G + 2) * 16; i += kAttnThreads) {
+      const int h = i >> 4, cc = i & 15;
+      dst[i] = __ldcg((h < G ? q + h * 16 : (h == G ? k : v)) + cc);
     }
   }
   __syncthreads();
   grid_launch_dependents();
+  for (int h = 0; h < G; ++h) sm.q_s[h * kQPitch + tid] = rope_dim(sm.raw + h * kHeadDim, tid, c, s);
+  const float kr = rope_dim(sm.raw + G * kHeadDim, tid, c, s);
+  const float vv = bf(sm.raw[(G + 1) * kHeadDim + tid]);
+  sm.kn_s[tid] = kr;
+  sm.vn_s[tid] = vv;
+  if (pos >= j0 && pos < j1) {  // this split owns the new position: store it
+    const size_t at = ((size_t)kvh * p.max_seq + pos) * kHeadDim + tid;
+    p.k_cache[at] = to_bf(kr);
+    p.v_cache[at] = to_bf(vv);
+  }
 
-  // Pass 1: scores s[j][h] = scale * q_h . k_j for this CTA's positions; warp
-  // w takes positions j0 + w, j0 + w + 4, ...; lane owns dims 4*lane..+3.
-  float wmax[16];
+  float o[16];  // o[h] for dimension tid
 #pragma unroll
-  for (int h = 0; h < 16; ++h) wmax[h] = -INFINITY;
-  const uint16_t* kc = p.k_cache + (size_t)kvh * p.max_seq * kHeadDim;
-  const uint16_t* vc = p.v_cache + (size_t)kvh * p.max_seq * kHeadDim;
-  for (int j = j0 + warp; j < j1; j += 4) {
-    float k4[4];
-    if (j == pos) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) k4[i] = kn_s[4 * lane + i];
-    } else {
-      const uint2 kv = __ldcg(reinterpret_cast<const uint2*>(kc + (size_t)j * kHeadDim + 4 * lane));
-      k4[0] = bf(kv.x & 0xffffu); k4[1] = bf(kv.x >> 16);
-      k4[2] = bf(kv.y & 0xffffu); k4[3] = bf(kv.y >> 16);
+  for (int h = 0; h < 16; ++h) o[h] = 0.f;
+
+  for (int t0 = j0; t0 < j1; t0 += kAttnTile) {
+    const int t1 = min(j1, t0 + kAttnTile);
+    if (t0 != j0) {
+      __syncthreads();  // the previous tile is consumed
+      load_tile(sm, kc, vc, t0, min(t1, pos), tid);
     }
+    __syncthreads();
+    const int n = t1 - t0;
+    for (int pi = tid; pi < n * G; pi += kAttnThreads) {  // scores
+      const int jl = pi / G, h = pi - jl * G;
+      const float* qh = sm.q_s + h * kQPitch;
+      float d = 0.f;
+      if (t0 + jl == pos) {
+        for (int e = 0; e < kHeadDim; ++e) d = fmaf(qh[e], sm.kn_s[e], d);
+      } else {
+        const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.kt_s + jl * kKPitch);
+#pragma unroll 8
+        for (int w = 0; w < kHeadDim / 2; ++w) {
+          const uint32_t kk = kw[w];
+          d = fmaf(qh[2 * w], bf(kk & 0xffffu), d);
+          d = fmaf(qh[2 * w + 1], bf(kk >> 16), d);
+        }
+      }
+      sm.sc_s[pi] = d * p.scale;
+    }
+    __syncthreads();
+    for (int h = warp; h < G; h += kAttnThreads / 32) {  // online softmax per head
+      float mx = -INFINITY;
+      for (int jl = lane; jl < n; jl += 32) mx = fmaxf(mx, sm.sc_s[jl * G + h]);
 #pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      if (h < G) {
-        const float4 q4 = *reinterpret_cast<const float4*>(q_s + h * kHeadDim + 4 * lane);
-        float d = q4.x * k4[0] + q4.y * k4[1] + q4.z * k4[2] + q4.w * k4[3];
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = sm.hm_s[h];
+      const float m_new = fmaxf(m_old, mx);
+      float sum = 0.f;
+      for (int jl = lane; jl < n; jl += 32) {
+        const float pr = __expf(sm.sc_s[jl * G + h] - m_new);
+        sm.sc_s[jl * G + h] = pr;
+        sum += pr;
+      }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-        d *= p.scale;
-        if (lane == 0) sc_s[(j - j0) * G + h] = d;
-        wmax[h] = fmaxf(wmax[h], d);
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane == 0) {
+        const float alpha = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
+        sm.ha_s[h] = alpha;
+        sm.hl_s[h] = sm.hl_s[h] * alpha + sum;
+        sm.hm_s[h] = m_new;
       }
     }
-  }
-  if (lane == 0) {
+    __syncthreads();
 #pragma unroll
     for (int h = 0; h < 16; ++h)
-      if (h < G) wm_s[warp * G + h] = wmax[h];
+      if (h < G) o[h] *= sm.ha_s[h];
+    for (int jl = 0; jl < n; ++jl) {  // P.V, thread tid owns dimension tid
+      const float vj = (t0 + jl == pos) ? sm.vn_s[tid] : bf(sm.vt_s[jl * kHeadDim + tid]);
+#pragma unroll
+      for (int h = 0; h < 16; ++h)
+        if (h < G) o[h] = fmaf(sm.sc_s[jl * G + h], vj, o[h]);
+    }
   }
-  __syncthreads();
-
-  // Pass 2: p = exp(s - m_h), l_h = sum p, o_h = sum p v_j.
-  float m_h[16];
+  // this split's partial (an empty split leaves m = -inf, l = 0, o = 0)
 #pragma unroll
   for (int h = 0; h < 16; ++h)
-    m_h[h] = (h < G) ? fmaxf(fmaxf(wm_s[h], wm_s[G + h]), fmaxf(wm_s[2 * G + h], wm_s[3 * G + h]))
-                     : 0.f;
-  float l_w[16], o_w[16][4];
-#pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    l_w[h] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o_w[h][i] = 0.f;
-  }
-  for (int j = j0 + warp; j < j1; j += 4) {
-    float v4[4];
-    if (j == pos) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) v4[i] = vn_s[4 * lane + i];
-    } else {
-      const uint2 vv = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)j * kHeadDim + 4 * lane));
-      v4[0] = bf(vv.x & 0xffffu); v4[1] = bf(vv.x >> 16);
-      v4[2] = bf(vv.y & 0xffffu); v4[3] = bf(vv.y >> 16);
-    }
-#pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      if (h < G) {
-        const float pr = __expf(sc_s[(j - j0) * G + h] - m_h[h]);
-        l_w[h] += pr;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o_w[h][i] = fmaf(pr, v4[i], o_w[h][i]);
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    if (h < G) {
-      if (lane == 0) wl_s[warp * G + h] = l_w[h];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) wo_s[(warp * G + h) * kHeadDim + 4 * lane + i] = o_w[h][i];
-    }
-  }
-  __syncthreads();
-  // CTA partial (all warps share m_h): fixed-order sum over the 4 warps.
-#pragma unroll
-  for (int h = 0; h < 16; ++h) {
-    if (h >= G) break;
-    po_s[h * kHeadDim + tid] = ((wo_s[(0 * G + h) * kHeadDim + tid] +
-                                 wo_s[(1 * G + h) * kHeadDim + tid]) +
-                                wo_s[(2 * G + h) * kHeadDim + tid]) +
-                               wo_s[(3 * G + h) * kHeadDim + tid];
-    if (tid == 0) {
-      pm_s[h] = m_h[h];
-      pl_s[h] = ((wl_s[h] + wl_s[G + h]) + wl_s[2 * G + h]) + wl_s[3 * G + h];
-    }
+    if (h < G) sm.po_s[h * kHeadDim + tid] = o[h];
+  if (tid < G) {
+    sm.pm_s[tid] = sm.hm_s[tid];
+    sm.pl_s[tid] = sm.hl_s[tid];
   }
 
   // Merge the splits of this KV head over DSMEM, in rank order.
@@ -252,23 +311,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   for (int idx = rank * kAttnThreads + tid; idx < G * kHeadDim; idx += kAttnThreads * kAttnSplits) {
     const int h = idx / kHeadDim;
     float M = -INFINITY;
-    for (int r = 0; r < kAttnSplits; ++r) M = fmaxf(M, cluster.map_shared_rank(pm_s, r)[h]);
+    for (int r = 0; r < kAttnSplits; ++r) M = fmaxf(M, cluster.map_shared_rank(sm.pm_s, r)[h]);
     float L = 0.f, O = 0.f;
     for (int r = 0; r < kAttnSplits; ++r) {
-      const float mr = cluster.map_shared_rank(pm_s, r)[h];
+      const float mr = cluster.map_shared_rank(sm.pm_s, r)[h];
       const float w = (mr == -INFINITY) ? 0.f : __expf(mr - M);
-      L = fmaf(w, cluster.map_shared_rank(pl_s, r)[h], L);
-      O = fmaf(w, cluster.map_shared_rank(po_s, r)[idx], O);
+      L = fmaf(w, cluster.map_shared_rank(sm.pl_s, r)[h], L);
+      O = fmaf(w, cluster.map_shared_rank(sm.po_s, r)[idx], O);
     }
     p.out[(size_t)(kvh * G + h) * kHeadDim + (idx - h * kHeadDim)] = to_bf(O / L);
   }
   cluster.sync();
-}
-
-static size_t attn_smem_bytes(int G, int max_seq) {
-  const int max_chunk = (max_seq + kAttnSplits - 1) / kAttnSplits;
-  return sizeof(float) * ((size_t)G * kHeadDim + 2 * kHeadDim + (size_t)max_chunk * G + 8 * G +
-                          4 * (size_t)G * kHeadDim + 2 * G + (size_t)G * kHeadDim);
 }
 
 int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_t,
@@ -287,7 +340,7 @@ int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_
   p.max_seq = max_seq;
   p.group = heads / kv_heads;
   p.scale = 1.0f / sqrtf((float)kHeadDim);
-  const size_t smem = attn_smem_bytes(p.group, max_seq);
+  const size_t smem = attn_smem_bytes(p.group);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)kv_heads, kAttnSplits, 1);
   cfg.blockDim = dim3(kAttnThreads);
@@ -307,7 +360,14 @@ int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_
 
 // ------------------------------------------------------------------ lm_head + argmax
 
-constexpr int kLmThreads = 256;
+// One persistent CTA per SM streams a contiguous range of embedding rows
+// (the tied lm_head) through a ring of shared-memory stages filled by 1-D
+// bulk copies; 8 consumer warps turn each stage's rows into logits.
+constexpr int kLmConsumerWarps = 8;
+constexpr int kLmThreads = (kLmConsumerWarps + 1) * 32;
+constexpr int kLmRowsPerStage = 16;
+// ring depth: 4 stages of 16 rows (192 KB at hidden 1536), 3 for hidden 2048
+__host__ __device__ constexpr int lm_stages(int hidden) { return hidden <= 1536 ? 4 : 3; }
 
 struct LmHeadWorkspace {
   unsigned long long best;  // (ordered bf16 logit << 32) | (0xffffffff - index)
@@ -323,98 +383,173 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+static size_t lm_smem_bytes(int hidden) {
+  return 128 + (size_t)lm_stages(hidden) * kLmRowsPerStage * hidden * 2 + (size_t)hidden * 4 +
+         2 * lm_stages(hidden) * sizeof(uint64_t);
+}
+
 template <int CH>  // CH = hidden / 256: 16-byte chunks per lane per row
-__global__ void __launch_bounds__(kLmThreads) lm_head_kernel(
+__global__ void __launch_bounds__(kLmThreads, 1) lm_head_kernel(
     const uint16_t* __restrict__ h, const uint16_t* __restrict__ norm_w, float eps,
     const uint16_t* __restrict__ embed, int vocab, uint16_t* __restrict__ logits,
-    int64_t* token, int64_t* pos, LmHeadWorkspace* ws) {
+    int64_t* token, int64_t* pos, LmHeadWorkspace* ws, int* err) {
   constexpr int H = CH * 256;
-  __shared__ float x_s[H];
-  __shared__ float red[kLmThreads / 32];
-  __shared__ unsigned long long best_s[kLmThreads / 32];
+  constexpr uint32_t kRowBytes = H * 2;
+  constexpr int kLmStages = lm_stages(H);
+  extern __shared__ __align__(128) unsigned char smem_lm[];
+  uint8_t* stage_s = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_lm) + 127) & ~static_cast<uintptr_t>(127));
+  float* x_s = reinterpret_cast<float*>(stage_s + kLmStages * kLmRowsPerStage * kRowBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_s + H);
+  uint64_t* empty = full + kLmStages;
+  __shared__ float red[kLmConsumerWarps];
+  __shared__ unsigned long long best_s[kLmConsumerWarps];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // Weights are constant: warm this CTA's first rows into L2 before waiting.
-  grid_dependency_wait();
-  // Final RMSNorm (fp32 normalisation, cast to bf16, times the bf16 weight).
-  float ss = 0.f;
-  for (int i = tid; i < H; i += kLmThreads) {
-    const float v = bf(h[i]);
-    ss = fmaf(v, v, ss);
+  // this CTA's rows
+  const int per = (vocab + gridDim.x - 1) / gridDim.x;
+  const int r0 = min(vocab, blockIdx.x * per), r1 = min(vocab, r0 + per);
+  const int n_stages = (r1 - r0 + kLmRowsPerStage - 1) / kLmRowsPerStage;
+
+  if (tid == 0) {
+    for (int s = 0; s < kLmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLmConsumerWarps);
+    }
+    fence_mbar_init();
   }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if (lane == 0) red[warp] = ss;
   __syncthreads();
-  float tot = 0.f;
-  for (int w = 0; w < kLmThreads / 32; ++w) tot += red[w];
-  const float inv = rsqrtf(tot / (float)H + eps);
-  for (int i = tid; i < H; i += kLmThreads) x_s[i] = rbf(rbf(bf(h[i]) * inv) * bf(norm_w[i]));
-  __syncthreads();
-  grid_launch_dependents();
 
-  // Lane l owns elements 8*(32*c + l) .. +7 of every row (coalesced 512 B per
-  // warp load); x for them stays in registers.
-  float xr[CH][8];
-#pragma unroll
-  for (int c = 0; c < CH; ++c)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) xr[c][i] = x_s[8 * (32 * c + lane) + i];
-
-  const int warps_total = gridDim.x * (kLmThreads / 32);
-  const int gw = blockIdx.x * (kLmThreads / 32) + warp;
   unsigned long long best = 0;
-  // two rows per warp iteration: 2*CH independent 16-byte loads in flight
-  for (int r = 2 * gw; r < vocab; r += 2 * warps_total) {
-    const int r1 = min(r + 1, vocab - 1);
-    uint4 a[CH], b[CH];
-    const uint4* ra = reinterpret_cast<const uint4*>(embed + (size_t)r * H);
-    const uint4* rb = reinterpret_cast<const uint4*>(embed + (size_t)r1 * H);
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      a[c] = __ldcs(ra + 32 * c + lane);
-      b[c] = __ldcs(rb + 32 * c + lane);
-    }
-    float da = 0.f, db = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const uint32_t* av = reinterpret_cast<const uint32_t*>(&a[c]);
-      const uint32_t* bv = reinterpret_cast<const uint32_t*>(&b[c]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        da = fmaf(bf(av[i] & 0xffffu), xr[c][2 * i], da);
-        da = fmaf(bf(av[i] >> 16), xr[c][2 * i + 1], da);
-        db = fmaf(bf(bv[i] & 0xffffu), xr[c][2 * i], db);
-        db = fmaf(bf(bv[i] >> 16), xr[c][2 * i + 1], db);
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      da += __shfl_xor_sync(0xffffffffu, da, off);
-      db += __shfl_xor_sync(0xffffffffu, db, off);
-    }
+  if (warp == kLmConsumerWarps) {
+    // producer: the embedding is constant, so it streams before the grid
+    // dependency is resolved
+    grid_launch_dependents();
     if (lane == 0) {
-      // argmax over the bf16 logits, first index among equals
-      const uint16_t la = to_bf(da), lb = to_bf(db);
-      if (logits) {
-        logits[r] = la;
-        if (r + 1 < vocab) logits[r + 1] = lb;
+      int slot = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int j = 0; j < n_stages; ++j) {
+        if (j >= kLmStages && !mbar_wait(&empty[slot], phase ^ 1u)) {
+          if (err) atomicCAS(err, 0, kErrEmptyWait);
+          break;
+        }
+        const int rs = r0 + j * kLmRowsPerStage;
+        const uint32_t bytes = (uint32_t)min(kLmRowsPerStage, r1 - rs) * kRowBytes;
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_load(stage_s + (size_t)slot * kLmRowsPerStage * kRowBytes,
+                  embed + (size_t)rs * H, bytes, &full[slot]);
+        ++issued;
+        if (++slot == kLmStages) {
+          slot = 0;
+          phase ^= 1u;
+        }
       }
-      const unsigned long long ka =
-          ((unsigned long long)order_key(bf(la)) << 32) | (0xffffffffu - (uint32_t)r);
-      best = ka > best ? ka : best;
-      if (r + 1 < vocab) {
-        const unsigned long long kb =
-            ((unsigned long long)order_key(bf(lb)) << 32) | (0xffffffffu - (uint32_t)(r + 1));
-        best = kb > best ? kb : best;
+      for (int j = max(0, issued - kLmStages); j < issued; ++j)  // no copy left in flight
+        if (!mbar_wait(&full[j % kLmStages], (j / kLmStages) & 1) && err)
+          atomicCAS(err, 0, kErrDrainWait);
+    }
+  } else {
+    grid_dependency_wait();  // h comes from the previous kernel
+    // final RMSNorm (fp32 normalisation, cast to bf16, times the bf16 weight)
+    float ss = 0.f;
+    for (int i = tid; i < H; i += kLmConsumerWarps * 32) {
+      const float v = bf(h[i]);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) red[warp] = ss;
+    asm volatile("bar.sync 1, %0;" ::"r"(kLmConsumerWarps * 32) : "memory");
+    float tot = 0.f;
+    for (int w = 0; w < kLmConsumerWarps; ++w) tot += red[w];
+    const float inv = rsqrtf(tot / (float)H + eps);
+    for (int i = tid; i < H; i += kLmConsumerWarps * 32)
+      x_s[i] = rbf(rbf(bf(h[i]) * inv) * bf(norm_w[i]));
+    asm volatile("bar.sync 1, %0;" ::"r"(kLmConsumerWarps * 32) : "memory");
+    grid_launch_dependents();  // every thread signals (the producer warp below)
+
+    // lane l owns elements 8*(32*c + l) .. +7 of every row
+    float xr[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xr[c][i] = x_s[8 * (32 * c + lane) + i];
+
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < n_stages; ++j) {
+      if (!mbar_wait(&full[slot], phase)) {
+        if (err) atomicCAS(err, 0, kErrFullWait);
+        break;
+      }
+      const int rs = r0 + j * kLmRowsPerStage;
+      const int nrows = min(kLmRowsPerStage, r1 - rs);
+      const uint8_t* st = stage_s + (size_t)slot * kLmRowsPerStage * kRowBytes;
+      // warp w takes rows w and w + 8 of the stage (two dot products in flight)
+      for (int rl = warp; rl < nrows; rl += 2 * kLmConsumerWarps) {
+        const int rl2 = rl + kLmConsumerWarps;
+        const bool two = rl2 < nrows;
+        const uint4* ra = reinterpret_cast<const uint4*>(st + (size_t)rl * kRowBytes);
+        const uint4* rb = reinterpret_cast<const uint4*>(st + (size_t)(two ? rl2 : rl) * kRowBytes);
+        float da = 0.f, db = 0.f;
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const uint4 a = ra[32 * c + lane], b = rb[32 * c + lane];
+          const uint32_t* av = reinterpret_cast<const uint32_t*>(&a);
+          const uint32_t* bv = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            da = fmaf(bf(av[i] & 0xffffu), xr[c][2 * i], da);
+            da = fmaf(bf(av[i] >> 16), xr[c][2 * i + 1], da);
+            db = fmaf(bf(bv[i] & 0xffffu), xr[c][2 * i], db);
+            db = fmaf(bf(bv[i] >> 16), xr[c][2 * i + 1], db);
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          da += __shfl_xor_sync(0xffffffffu, da, off);
+          db += __shfl_xor_sync(0xffffffffu, db, off);
+        }
+        if (lane == 0) {
+          // argmax over the bf16 logits, first index among equals
+          const int ia = rs + rl, ib = rs + rl2;
+          const uint16_t la = to_bf(da);
+          if (logits) logits[ia] = la;
+          const unsigned long long ka =
+              ((unsigned long long)order_key(bf(la)) << 32) | (0xffffffffu - (uint32_t)ia);
+          best = ka > best ? ka : best;
+          if (two) {
+            const uint16_t lb = to_bf(db);
+            if (logits) logits[ib] = lb;
+            const unsigned long long kb =
+                ((unsigned long long)order_key(bf(lb)) << 32) | (0xffffffffu - (uint32_t)ib);
+            best = kb > best ? kb : best;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == kLmStages) {
+        slot = 0;
+        phase ^= 1u;
       }
     }
+    if (lane == 0) best_s[warp] = best;
   }
-  if (lane == 0) best_s[warp] = best;
   __syncthreads();
   if (tid == 0) {
     unsigned long long b = 0;
-    for (int w = 0; w < kLmThreads / 32; ++w) b = best_s[w] > b ? best_s[w] : b;
+    for (int w = 0; w < kLmConsumerWarps; ++w) b = best_s[w] > b ? best_s[w] : b;
     atomicMax(&ws->best, b);
     __threadfence();
     const unsigned int ticket = atomicAdd(&ws->done, 1u);
@@ -435,11 +570,16 @@ int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const vo
                           void* workspace, int pdl, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const int sms = device_info(dev).sm_count > 0 ? device_info(dev).sm_count : 148;
+  const DeviceInfo& di = device_info(dev);
+  const int sms = di.sm_count > 0 ? di.sm_count : 148;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * sms));
+  cfg.gridDim = dim3((unsigned)sms);
   cfg.blockDim = dim3(kLmThreads);
+  cfg.dynamicSmemBytes = lm_smem_bytes(hidden);
   cfg.stream = stream;
+  if (cfg.dynamicSmemBytes > (size_t)di.max_smem_optin)
+    return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden %d needs %zu B of shared memory",
+                hidden, cfg.dynamicSmemBytes);
   cudaLaunchAttribute at = pdl_attr(pdl);
   cfg.attrs = &at;
   cfg.numAttrs = 1;
@@ -448,15 +588,17 @@ int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const vo
   const uint16_t* em = static_cast<const uint16_t*>(embed);
   uint16_t* lg = static_cast<uint16_t*>(logits);
   LmHeadWorkspace* ws = static_cast<LmHeadWorkspace*>(workspace);
+  int* err = di.err_word;
   cudaError_t e;
   switch (hidden / 256) {
-    case 1: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<1>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    case 2: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<2>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    case 4: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<4>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    case 6: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<6>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    case 8: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<8>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    case 16: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<16>, hh, nw, eps, em, vocab, lg, token, pos, ws); break;
-    default: return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden %d not in {256, 512, 1024, 1536, 2048, 4096}", hidden);
+    case 1: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<1>, hh, nw, eps, em, vocab, lg, token, pos, ws, err); break;
+    case 2: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<2>, hh, nw, eps, em, vocab, lg, token, pos, ws, err); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<4>, hh, nw, eps, em, vocab, lg, token, pos, ws, err); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<6>, hh, nw, eps, em, vocab, lg, token, pos, ws, err); break;
+    case 8: e = cudaLaunchKernelEx(&cfg, lm_head_kernel<8>, hh, nw, eps, em, vocab, lg, token, pos, ws, err); break;
+    default:
+      return fail(W4_ERR_UNSUPPORTED,
+                  "w4_lm_head_argmax: hidden %d not in {256, 512, 1024, 1536, 2048}", hidden);
   }
   return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_lm_head_argmax launch");
 }
@@ -508,7 +650,25 @@ int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const vo
 }
 
 int decode_init_device(const DeviceInfo& di) {
-  const size_t smem = attn_smem_bytes(16, 16384);
+  const int lm_smem = (int)std::min<size_t>(lm_smem_bytes(2048), (size_t)di.max_smem_optin);
+  const void* lm_kernels[] = {(const void*)lm_head_kernel<1>, (const void*)lm_head_kernel<2>,
+                              (const void*)lm_head_kernel<4>, (const void*)lm_head_kernel<6>,
+                              (const void*)lm_head_kernel<8>};
+  for (const void* k : lm_kernels) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, lm_smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lm_head smem)");
+  }
+  // the same carveout as the GEMV kernels, so PDL-chained grids share SMs
+  const void* all[] = {(const void*)lm_head_kernel<1>, (const void*)lm_head_kernel<2>,
+                       (const void*)lm_head_kernel<4>, (const void*)lm_head_kernel<6>,
+                       (const void*)lm_head_kernel<8>, (const void*)attention_kernel,
+                       (const void*)embed_kernel};
+  for (const void* k : all) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
+  }
+  const size_t smem = attn_smem_bytes(16);
   cudaError_t e = cudaFuncSetAttribute(attention_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)std::min<size_t>(smem, (size_t)di.max_smem_optin));

@@ -74,45 +74,37 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Applies the staging transform to 8 consecutive activations x[m, k..k+7]:
-//   RMSNorm: round(round(x * inv_rms[m]) * w[k])   (Qwen2/Llama RMSNorm: fp32
-//            normalisation, cast to the activation type, times the weight)
-//   SwiGLU : round(round(silu(g)) * u) with g = x[m, k], u = x[m, K + k] of a
-//            [M, 2K] gate|up row (silu in fp32, cast, product cast)
+// Applies the staging transform to 8 consecutive activations x[m, k..k+7]
+// (aux holds the matching 8 values of the second operand, loaded by the
+// caller in the same batch as x):
+//   RMSNorm: round(round(x * inv_rms) * w[k])   aux = w[k..k+7] (Qwen2/Llama
+//            RMSNorm: fp32 normalisation, cast to the activation type, times
+//            the weight)
+//   SwiGLU : round(round(silu(g)) * u)           x = gate, aux = up (silu in
+//            fp32, cast; product cast)
 template <bool kBF16>
-__device__ __forceinline__ uint4 stage_transform(const GemvParams& p, int m, int k, uint4 v,
-                                                 float inv_rms) {
-  if (p.pro == W4_PRO_RMSNORM) {
-    const uint4 wv = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.pro_w) + k));
-    const uint32_t* xi = reinterpret_cast<const uint32_t*>(&v);
-    const uint32_t* wi = reinterpret_cast<const uint32_t*>(&wv);
-    uint4 o;
-    uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+__device__ __forceinline__ uint4 stage_transform(int pro, uint4 v, uint4 aux, float inv_rms) {
+  const uint32_t* xi = reinterpret_cast<const uint32_t*>(&v);
+  const uint32_t* ai = reinterpret_cast<const uint32_t*>(&aux);
+  uint4 o;
+  uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+  if (pro == W4_PRO_RMSNORM) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 xf = h2f2(xi[i], kBF16), wf = h2f2(wi[i], kBF16);
+      const float2 xf = h2f2(xi[i], kBF16), wf = h2f2(ai[i], kBF16);
       oi[i] = pack2(round_to(xf.x * inv_rms, kBF16) * wf.x,
                     round_to(xf.y * inv_rms, kBF16) * wf.y, kBF16);
     }
     return o;
   }
-  if (p.pro == W4_PRO_SWIGLU) {
-    const uint16_t* row = static_cast<const uint16_t*>(p.x) + (size_t)m * 2 * p.K;
-    const uint4 uv = __ldcg(reinterpret_cast<const uint4*>(row + p.K + k));
-    const uint32_t* gi = reinterpret_cast<const uint32_t*>(&v);
-    const uint32_t* ui = reinterpret_cast<const uint32_t*>(&uv);
-    uint4 o;
-    uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 g = h2f2(gi[i], kBF16), u = h2f2(ui[i], kBF16);
-      const float sa = round_to(g.x / (1.0f + __expf(-g.x)), kBF16);
-      const float sb = round_to(g.y / (1.0f + __expf(-g.y)), kBF16);
-      oi[i] = pack2(sa * u.x, sb * u.y, kBF16);
-    }
-    return o;
+  for (int i = 0; i < 4; ++i) {
+    const float2 g = h2f2(xi[i], kBF16), u = h2f2(ai[i], kBF16);
+    const float sa = round_to(g.x / (1.0f + __expf(-g.x)), kBF16);
+    const float sb = round_to(g.y / (1.0f + __expf(-g.y)), kBF16);
+    oi[i] = pack2(sa * u.x, sb * u.y, kBF16);
   }
-  return v;
+  return o;
 }
 
 template <int SW, int RG>
@@ -200,6 +192,11 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     tma_prefetch_desc(&tm_s);
   }
   __syncthreads();
+  // Every thread signals at once: the next grid of a PDL chain is scheduled as
+  // soon as there is room on the SMs (shared memory bounds the overlap to about
+  // two grids per SM), streams its weights while this one runs, and reads our
+  // output only after its own grid-dependency wait.
+  grid_launch_dependents();
 
   // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
   // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
@@ -213,6 +210,9 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
 
   if (warp == T::kCW) {
     // ------------------------------------------------------------ producer
+    // The launch of a dependent (PDL) grid waits until every thread of every
+    // CTA here has signalled; lanes 1..31 signal at once, lane 0 once all of
+    // this CTA's weight loads are in flight.
     if (lane == 0) {
       int issued = 0;
       int slot = 0;
@@ -235,14 +235,11 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
           phase ^= 1u;
         }
       }
-      // All of this CTA's weight loads are in flight: dependent grids may be
-      // scheduled and start their own weight streams (they read this grid's
-      // output only after their grid-dependency wait).
-      grid_launch_dependents();
       // Do not leave while copies into this CTA's shared memory are in flight.
       for (int j = max(0, issued - S); j < issued; ++j)
         if (!mbar_wait(&full[j % S], (j / S) & 1)) report_error(p.err, kErrDrainWait);
     }
+
   } else {
     // ------------------------------------------------------------ consumers
     const int nct = T::kCW * 32;
@@ -251,7 +248,13 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     const uint16_t* xg = static_cast<const uint16_t*>(p.x);
     // x row pitch: a SwiGLU prologue reads gate|up rows of 2K
     const size_t x_pitch = (p.pro == W4_PRO_SWIGLU) ? 2 * (size_t)p.K : (size_t)p.K;
-    if (p.pro == W4_PRO_RMSNORM) {
+    // RMSNorm needs 1/rms of the whole row. When this CTA stages the whole row
+    // of a single activation row in one batch (the decode case), the sum of
+    // squares comes from the staging loads themselves (one global round
+    // trip); otherwise a pre-pass over the row computes it first.
+    const bool rms_one_pass = p.pro == W4_PRO_RMSNORM && M == 1 && g0 == 0 &&
+                              g1 == p.groups_total && rows_slice <= 4 * nct;
+    if (p.pro == W4_PRO_RMSNORM && !rms_one_pass) {
       // inv_rms[m] over the whole row (every CTA recomputes it: K <= 28672
       // activations, served from L2), reduced in a fixed order
       float* s_part = s_red;  // scratch: [kCW][M] partial sums (s_red is free until the epilogue)
@@ -288,18 +291,48 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     // b0 is the same for every consumer thread, so all of them run the same
     // trips and every shuffle below has its full warp
     for (int b0 = 0; b0 < total; b0 += 4 * nct) {
-      uint4 v[4];
+      uint4 v[4], aux[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int idx = b0 + u * nct + threadIdx.x;
         v[u] = make_uint4(0u, 0u, 0u, 0u);
+        aux[u] = make_uint4(0u, 0u, 0u, 0u);
         if (idx < total) {
           const int m = idx / rows_slice;
           const int krow = g0 * 16 + (idx - m * rows_slice);  // packed row = 8 activations
-          if (krow < g1 * 16)
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(xg + (size_t)m * x_pitch +
-                                                          (size_t)krow * 8));
+          if (krow < g1 * 16) {
+            const uint16_t* xr = xg + (size_t)m * x_pitch + (size_t)krow * 8;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(xr));
+            if (p.pro == W4_PRO_RMSNORM)
+              aux[u] = __ldg(reinterpret_cast<const uint4*>(
+                  static_cast<const uint16_t*>(p.pro_w) + (size_t)krow * 8));
+            else if (p.pro == W4_PRO_SWIGLU)
+              aux[u] = __ldcg(reinterpret_cast<const uint4*>(xr + p.K));
+          }
         }
+      }
+      if (rms_one_pass) {  // sum of squares of the (whole, single) row from registers
+        float acc2 = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v[u]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = h2f2(vi[e], kBF16);
+            acc2 = fmaf(f.x, f.x, acc2);
+            acc2 = fmaf(f.y, f.y, acc2);
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+        if (lane == 0) s_red[warp] = acc2;
+        consumer_bar_sync(nct);
+        if (threadIdx.x == 0) {
+          float tot = 0.f;
+          for (int w = 0; w < T::kCW; ++w) tot += s_red[w];
+          s_inv[0] = rsqrtf(tot / (float)p.K + p.eps);
+        }
+        consumer_bar_sync(nct);
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -312,7 +345,8 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
           const int r = idx - m * rows_slice;
           const int krow = g0 * 16 + r;
           if (p.pro != W4_PRO_NONE && krow < g1 * 16)
-            v[u] = stage_transform<kBF16>(p, m, krow * 8, v[u], p.pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
+            v[u] = stage_transform<kBF16>(p.pro, v[u], aux[u],
+                                          p.pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
           o = permute_row<kBF16>(v[u]);
           *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
           const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
@@ -623,6 +657,11 @@ int gemv_init_device(const DeviceInfo& di) {
           if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max smem)");
           e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
           if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(cluster)");
+          // One carveout for every kernel of the library: CTAs of a dependent
+          // (PDL) grid can then share SMs with the grid still finishing.
+          e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   cudaSharedmemCarveoutMaxShared);
+          if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
         }
   return W4_OK;
 }

@@ -2,10 +2,11 @@
 
 The reference timed num_warps in {4, 8} with a fresh zeroed output per trial,
 because its split-K kernel accumulated with atomics (kernels.py:154-159). The
-kernel here writes its output without atomics, so trials can share buffers;
-what matters instead is that B200's 126 MB L2 would hold every decode-sized
-weight matrix, so every timed launch is preceded by a write of twice the L2
-size: the tuner ranks tiles for weights streamed from HBM, as in decode.
+kernel here writes its output without atomics, so trials can share buffers.
+What matters instead: B200's 126 MB L2 would hold every decode-sized weight
+matrix, and a lone microsecond launch cannot be timed with events. So each
+candidate tile is timed as a CUDA graph of dependent launches, each on its own
+weight copy (the copies exceed 3x L2), as the GEMVs of a decode step run.
 Tuning must run outside CUDA-graph capture (it synchronises).
 """
 from __future__ import annotations
@@ -53,49 +54,70 @@ def _candidates(M: int, K: int, N: int, split_k: int | None, num_warps: int | No
         yield d
 
 
-def time_config(x2, packed, scales, y, cfg: GemvConfig, flush: torch.Tensor,
-                reps: int = 9, warmup: int = 2) -> float:
-    """Median device time (us) of one launch with a cold L2."""
+def chain_length(weight_bytes: int, l2_bytes: int) -> int:
+    """Launches per timed chain: enough distinct weight copies to exceed 3x L2."""
+    return int(min(256, max(8, -(-3 * l2_bytes // max(1, weight_bytes)))))
+
+
+def time_config(x2, pool, y, cfg: GemvConfig, reps: int = 3) -> float:
+    """Per-launch device time (us) of `cfg` in a chain of dependent launches.
+
+    The chain is one CUDA graph of len(pool) launches, each on its own copy
+    of the weights (so every launch streams from HBM) and chained with
+    programmatic dependent launch, the way a decode step issues its GEMVs.
+    The best of `reps` replays is taken; a single launch is never timed alone
+    (event timestamps are too coarse for microsecond kernels).
+    """
     from .kernels import gemv_launch
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(reps)]
-    for _ in range(warmup):
-        gemv_launch(x2, packed, scales, y, cfg)
-    for i in range(reps):
-        flush.sum()  # evict the weights with clean lines (a write would leave dirty
-        starts[i].record()  # lines whose write-back competes with the timed reads)
-        gemv_launch(x2, packed, scales, y, cfg)
-        ends[i].record()
-    torch.cuda.synchronize()
-    return statistics.median(s.elapsed_time(e) * 1e3 for s, e in zip(starts, ends))
-
-
-def flush_buffer(device: torch.device) -> torch.Tensor:
-    l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    return torch.zeros(max(2 * l2, 64 << 20) // 4, dtype=torch.float32, device=device)
+    c = GemvConfig(cfg.strips, cfg.row_groups, cfg.stages, cfg.split, 1)
+    stream = torch.cuda.Stream(x2.device)
+    with torch.cuda.stream(stream):
+        gemv_launch(x2, *pool[0], y, c)  # validates the config before capture
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for packed, scales in pool:
+                gemv_launch(x2, packed, scales, y, c)
+    best = float("inf")
+    with torch.cuda.stream(stream):
+        g.replay()  # upload
+        for _ in range(reps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            b.synchronize()
+            best = min(best, a.elapsed_time(b) * 1e3 / len(pool))
+    del g
+    return best
 
 
 def tune_gemv(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dtype,
               split_k: int | None, num_warps: int | None, device: torch.device,
               return_table: bool = False):
-    """Times every candidate tile and returns the fastest GemvConfig."""
+    """Times every candidate tile (in dependent chains) and returns the fastest."""
     with torch.cuda.device(device):
         gen = torch.Generator(device=device).manual_seed(1234)
         packed = torch.randint(-2**31, 2**31 - 1, (K // 8, N), generator=gen, dtype=torch.int32,
                                device=device)
         scales = (torch.rand((K // 128, N), generator=gen, device=device) * 0.01 + 1e-3).half()
+        l2 = torch.cuda.get_device_properties(device).L2_cache_size
+        n = chain_length(packed.numel() * 4 + scales.numel() * 2, l2)
+        pool = [(packed.clone(), scales.clone()) for _ in range(n - 1)] + [(packed, scales)]
         x2 = torch.randn((M, K), generator=gen, device=device).to(x_dtype)
         y = torch.empty((M, N), dtype=y_dtype, device=device)
-        flush = flush_buffer(device)
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         table = []
         for cfg in _candidates(M, K, N, split_k, num_warps, sms):
             try:
-                us = time_config(x2, packed, scales, y, cfg, flush)
+                us = time_config(x2, pool, y, cfg)
             except (ValueError, NotImplementedError, RuntimeError):
                 continue  # tile does not fit (shared memory, cluster size)
             table.append((us, cfg.as_tuple()))
+        del pool
         if not table:
             raise RuntimeError(f"no GEMV tile could be launched for M={M} K={K} N={N}")
         table.sort()
