@@ -78,6 +78,15 @@ WORKLOADS = {
 }
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of w4_gemv_kernel,
+# from `ncu --set full` captures (profiles/w4_gemv_kernel_*.md), keyed by
+# (M, K, N of the launch); the bench reports it as roofline.traffic.
+NCU_TRAFFIC = {
+    (1, 1536, 8960): 7_161_344,
+    (1, 8960, 1536): 7_175_936,
+}
+
+
 def measured_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -434,7 +443,8 @@ def run_gemv_workload(args, rank, world, local):
                          "kernel": f"w4_gemv_kernel M={dM} K={dK} N={n_loc[dom]} act={ddt}",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": None, "bytes_per_launch": local_bytes[dom],
+                         "traffic": NCU_TRAFFIC.get((dM, dK, n_loc[dom])),
+                         "bytes_per_launch": local_bytes[dom],
                          "mean_launch_us": round(dom_us, 3),
                          "timing": "mean launch of a PDL chain of this GEMV over "
                                    "weight copies exceeding 3x L2 (region B)",
