@@ -233,6 +233,7 @@ def cpu_sample(cases_spec, seconds):
     """GB/s of the CPU restatement over whole passes for about `seconds`."""
     from oracle import c_oracle
 
+    c_oracle.use_all_cores()
     cases = cpu_cases(cases_spec)
     cpu_pass(cases)  # warm the OpenMP pool and the pages
     passes, t0 = 0, time.perf_counter()
@@ -249,6 +250,7 @@ def run_reference(args, rank, world):
         return
     from oracle import c_oracle
 
+    c_oracle.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
     wl = WORKLOADS["sweep" if args.workload == "decode" else args.workload]
     cases = cpu_cases(wl["cases"])
     for _ in range(args.warmup):

@@ -26,6 +26,8 @@ def lib() -> ctypes.CDLL:
         L.w4o_dequant_matmul.argtypes = [P, i, i, P, P, i, i, P, P]
         L.w4o_gemv_exact.argtypes = [P, i, i, P, P, i, i, P]
         L.w4o_max_threads.restype = i
+        L.w4o_set_threads.argtypes = [i]
+        L.w4o_set_threads.restype = i
         _lib = L
     return _lib
 
@@ -80,3 +82,11 @@ def gemv_exact(x: np.ndarray, packed: np.ndarray, scales: np.ndarray,
 
 def max_threads() -> int:
     return lib().w4o_max_threads()
+
+
+def use_all_cores() -> int:
+    """Lets the OpenMP regions use every host core the process may run on."""
+    import os
+
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return lib().w4o_set_threads(int(n or 1))

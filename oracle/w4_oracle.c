@@ -51,6 +51,18 @@ int w4o_max_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP thread count of the following parallel regions (a process
+   launcher may have set OMP_NUM_THREADS=1); returns the new maximum. */
+int w4o_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
+
 /* nan_as_cpu: 0 -> q = 0 where w/s is NaN (torch on a CUDA device),
  *             1 -> q = INT32_MIN (torch on x86), summed in int64 and wrapped. */
 void w4o_pack(const uint16_t* w, int K, int N, int group_size, int nan_as_cpu,
