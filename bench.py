@@ -549,7 +549,7 @@ def run_decode(args, rank, world, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peak, peak_kind = measured_peaks()
-    model = W4DecodeModel(device=device, seed=0)
+    model = W4DecodeModel(device=device, seed=0, mode=args.decode_mode)
     model.capture()
     prompt_len = 32
     g = torch.Generator().manual_seed(0)
@@ -607,8 +607,11 @@ def run_decode(args, rank, world, local):
         "config": {"workload": "Qwen2.5-1.5B architecture decode, 28 layers, hidden 1536, "
                                "int4 linears, tied bf16 lm_head 1536x151936, static KV 2048",
                    "prompt": prompt_len, "global_batch": world,
-                   "parallelism": f"replicas{world}"},
-        "gpu_launches": (2 + 5 * model.cfg.layers) * args.steps,
+                   "parallelism": f"replicas{world}",
+                   "step": ("one persistent cooperative kernel (w4_decode_step)"
+                            if args.decode_mode == "mega" else
+                            "142 PDL-chained kernels (embed, 5 per layer, lm_head)")},
+        "gpu_launches": model.launches_per_step() * args.steps,
         "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -633,6 +636,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode"], default="sweep")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--decode-mode", choices=["mega", "fused"], default="fused",
+                    help="decode workload: the step as one kernel or as 142 kernels")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

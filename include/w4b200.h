@@ -188,6 +188,55 @@ int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
                              void* logits, int64_t* token, int64_t* pos,
                              int pdl, void* stream);
 
+/* ---------------------------------------------------------------------
+ * The whole decode step as one persistent kernel.
+ *
+ * Replaces the per-token model forward of scripts/decode_loop.py:106-124
+ * (HF forward + argmax + .item()) with one cooperative launch per token:
+ * embedding, every layer (RMSNorm, q|k|v, RoPE, KV write, attention, o,
+ * RMSNorm, gate|up, SwiGLU, down, residuals), final RMSNorm, tied lm_head
+ * and argmax. The int4 weights use the reference packing
+ * (src/roofline/kernels.py:24-47) stacked over layers: packed
+ * [layers * K/8, N], scales [layers * K/128, N]. All other tensors are bf16.
+ * Needs head_dim 128, heads / kv_heads <= 8 and hidden in {256, 512, 1024,
+ * 1536, 2048}. */
+typedef struct w4_decode_model {
+  int layers, hidden, intermediate, heads, kv_heads, head_dim, vocab, max_seq;
+  float eps;                       /* RMSNorm epsilon */
+  const int32_t* qkv_packed;       /* [layers*hidden/8, hidden + 2*kv_heads*128] */
+  const void* qkv_scales;
+  const int32_t* o_packed;         /* [layers*hidden/8, hidden] */
+  const void* o_scales;
+  const int32_t* gu_packed;        /* [layers*hidden/8, 2*intermediate] (gate | up) */
+  const void* gu_scales;
+  const int32_t* down_packed;      /* [layers*intermediate/8, hidden] */
+  const void* down_scales;
+  const void* qkv_bias;            /* [layers, hidden + 2*kv_heads*128] */
+  const void* in_norm;             /* [layers, hidden] */
+  const void* post_norm;           /* [layers, hidden] */
+  const void* final_norm;          /* [hidden] */
+  const void* embed;               /* [vocab, hidden], also the lm_head */
+  const void* cos_table;           /* [max_seq, 128] */
+  const void* sin_table;           /* [max_seq, 128] */
+  void* k_cache;                   /* [layers, kv_heads, max_seq, 128] */
+  void* v_cache;
+  const int64_t* prompt;           /* prompt ids; position p < *prompt_len reads prompt[p] */
+  const int64_t* prompt_len;
+  int64_t* token;                  /* in: previous argmax; out: this step's argmax */
+  int64_t* pos;                    /* in: position of this step; out: pos + 1 */
+  void* logits;                    /* [vocab] bf16, may be NULL */
+} w4_decode_model;
+
+/* Bytes of device scratch w4_decode_step needs for this model on the
+ * current device (zeroed once by the caller, 256-byte aligned). */
+int w4_decode_step_scratch_bytes(const w4_decode_model* model, size_t* bytes);
+
+/* One greedy decode step. The step's grid barriers are bounded waits: if one
+ * gives up, w4_device_error reports it and the scratch must be zeroed again
+ * before the next step. */
+int w4_decode_step(const w4_decode_model* model, void* scratch, size_t scratch_bytes,
+                   void* stream);
+
 /* Reads and clears the device-side error word that kernels set when a
  * bounded wait gives up (0 = no error). Synchronises the device. */
 int w4_device_error(int device, int* code);

@@ -65,6 +65,17 @@ class FusedOps(ctypes.Structure):
 _c_int, _c_void_p, _c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
 
 # name -> (restype, argtypes); must match include/w4b200.h
+class DecodeModel(ctypes.Structure):
+    """w4_decode_model: dimensions and device pointers of one decoder."""
+    _fields_ = [(n, ctypes.c_int) for n in ("layers", "hidden", "intermediate", "heads",
+                                            "kv_heads", "head_dim", "vocab", "max_seq")] + [
+        ("eps", ctypes.c_float)] + [(n, ctypes.c_void_p) for n in (
+            "qkv_packed", "qkv_scales", "o_packed", "o_scales", "gu_packed", "gu_scales",
+            "down_packed", "down_scales", "qkv_bias", "in_norm", "post_norm", "final_norm",
+            "embed", "cos_table", "sin_table", "k_cache", "v_cache", "prompt", "prompt_len",
+            "token", "pos", "logits")]
+
+
 SIGNATURES = {
     "w4_version": (_c_int, []),
     "w4_status_string": (ctypes.c_char_p, [_c_int]),
@@ -94,6 +105,9 @@ SIGNATURES = {
     "w4_lm_head_argmax_static": (_c_int, [_c_void_p, _c_void_p, ctypes.c_float, _c_void_p,
                                           _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
                                           _c_void_p]),
+    "w4_decode_step_scratch_bytes": (_c_int, [ctypes.POINTER(DecodeModel),
+                                              ctypes.POINTER(_c_size_t)]),
+    "w4_decode_step": (_c_int, [ctypes.POINTER(DecodeModel), _c_void_p, _c_size_t, _c_void_p]),
     "w4_device_error": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
 }
 

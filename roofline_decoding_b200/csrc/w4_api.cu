@@ -91,6 +91,7 @@ int init_locked(int device) {
     di.err_word = static_cast<int*>(addr);
     st = gemv_init_device(di);
     if (st == W4_OK) st = decode_init_device(di);
+    if (st == W4_OK) st = mega_init_device(di);
   } while (false);
   if (prev != device) cudaSetDevice(prev);
   if (st == W4_OK) {
@@ -322,6 +323,17 @@ int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
   if (st != W4_OK) return st;
   return lm_head_argmax_static(h, norm_weight, eps, embed, vocab, hidden, logits, token, pos,
                                pdl, (cudaStream_t)stream);
+}
+
+int w4_decode_step_scratch_bytes(const w4_decode_model* model, size_t* bytes) {
+  if (!model || !bytes) return fail(W4_ERR_INVALID_ARG, "w4_decode_step_scratch_bytes: null");
+  return decode_step_scratch_bytes(*model, bytes);
+}
+
+int w4_decode_step(const w4_decode_model* model, void* scratch, size_t scratch_bytes,
+                   void* stream) {
+  if (!model) return fail(W4_ERR_INVALID_ARG, "w4_decode_step: null model");
+  return launch_decode_step(*model, scratch, scratch_bytes, (cudaStream_t)stream);
 }
 
 int w4_device_error(int device, int* code) {

@@ -64,6 +64,12 @@ int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const vo
                           int pdl, cudaStream_t stream);
 int decode_init_device(const DeviceInfo& di);
 
+// Whole-step persistent kernel (w4_mega.cu).
+int mega_init_device(const DeviceInfo& di);
+int decode_step_scratch_bytes(const w4_decode_model& m, size_t* bytes);
+int launch_decode_step(const w4_decode_model& m, void* scratch, size_t scratch_bytes,
+                       cudaStream_t stream);
+
 // Tensor-map encoder resolved from the driver at init.
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,

@@ -18,6 +18,7 @@ the gate*up product in bf16, residual adds in bf16.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -78,29 +79,56 @@ def _rand(shape, gen, device, std):
 class W4DecodeModel:
     """Static-KV, graph-captured batch-1 greedy decoder with int4 linears."""
 
+    MODES = ("mega", "fused", "torch")
+
     def __init__(self, cfg: DecodeConfig = QWEN25_15B, device: str | torch.device = "cuda",
-                 seed: int = 0, std: float = 0.02, keep_dense: bool = False, fused: bool = True):
+                 seed: int = 0, std: float = 0.02, keep_dense: bool = False, fused: bool = True,
+                 mode: str | None = None):
+        """mode: "mega" (the step as one persistent kernel, w4_decode_step), "fused"
+        (142 PDL-chained kernels) or "torch" (torch ops around the fused GEMVs);
+        without it, `fused` picks "fused" or "torch"."""
         self.cfg = cfg
-        self.fused = fused
+        self.mode = mode or ("fused" if fused else "torch")
+        if self.mode not in self.MODES:
+            raise ValueError(f"mode must be one of {self.MODES}, got {self.mode!r}")
+        self.fused = self.mode != "torch"
         self.device = torch.device(device)
         self.dtype = torch.bfloat16
         gen = torch.Generator(device=self.device).manual_seed(seed)
         h, kv, inter = cfg.hidden, cfg.kv_dim, cfg.intermediate
         bf = self.dtype
+        nl = cfg.layers
+        # int4 weights stacked over layers ([layers * K/8, N] / [layers * K/128, N]);
+        # each layer uses row views of them
+        shapes = {"qkv": (h, h + 2 * kv), "o": (h, h), "gu": (h, 2 * inter), "down": (inter, h)}
+        self.w4 = {k: (torch.empty((nl * K // 8, N), dtype=torch.int32, device=self.device),
+                       torch.empty((nl * K // 128, N), dtype=torch.float16, device=self.device))
+                   for k, (K, N) in shapes.items()}
+        self.b_qkv = torch.empty((nl, h + 2 * kv), dtype=bf, device=self.device)
+        self.in_norms = torch.empty((nl, h), dtype=bf, device=self.device)
+        self.post_norms = torch.empty((nl, h), dtype=bf, device=self.device)
         self.layers = []
         self.dense: list[DenseLayer] | None = [] if keep_dense else None
-        for _ in range(cfg.layers):
+        for li in range(nl):
             w_qkv = _rand((h, h + 2 * kv), gen, self.device, std).half()
             w_o = _rand((h, h), gen, self.device, std).half()
             w_gu = _rand((h, 2 * inter), gen, self.device, std).half()
             w_down = _rand((inter, h), gen, self.device, std).half()
-            layer = {
-                "qkv": pack_weights(w_qkv), "o": pack_weights(w_o),
-                "gu": pack_weights(w_gu), "down": pack_weights(w_down),
-                "b_qkv": _rand((h + 2 * kv,), gen, self.device, 0.02).to(bf),
-                "in_norm": (1.0 + _rand((h,), gen, self.device, 0.05)).to(bf),
-                "post_norm": (1.0 + _rand((h,), gen, self.device, 0.05)).to(bf),
-            }
+            layer = {}
+            for name, w in (("qkv", w_qkv), ("o", w_o), ("gu", w_gu), ("down", w_down)):
+                K = shapes[name][0]
+                pk, sc = pack_weights(w)
+                dp = self.w4[name][0][li * K // 8:(li + 1) * K // 8]
+                ds = self.w4[name][1][li * K // 128:(li + 1) * K // 128]
+                dp.copy_(pk)
+                ds.copy_(sc)
+                layer[name] = (dp, ds)
+            self.b_qkv[li].copy_(_rand((h + 2 * kv,), gen, self.device, 0.02).to(bf))
+            self.in_norms[li].copy_((1.0 + _rand((h,), gen, self.device, 0.05)).to(bf))
+            self.post_norms[li].copy_((1.0 + _rand((h,), gen, self.device, 0.05)).to(bf))
+            layer["b_qkv"] = self.b_qkv[li]
+            layer["in_norm"] = self.in_norms[li]
+            layer["post_norm"] = self.post_norms[li]
             self.layers.append(layer)
             if keep_dense:
                 self.dense.append(DenseLayer(w_qkv, layer["b_qkv"], w_o, w_gu, w_down,
@@ -135,6 +163,36 @@ class W4DecodeModel:
         self.ws = torch.zeros((int(_lib.load().w4_lm_head_workspace_bytes()),), dtype=torch.uint8,
                               device=self.device)
         self._cfgs: dict | None = None
+        self._desc: _lib.DecodeModel | None = None
+        self.scratch: torch.Tensor | None = None
+        if self.mode == "mega":
+            self._init_mega()
+
+    def _init_mega(self) -> None:
+        """The w4_decode_model descriptor and the step's scratch."""
+        cfg = self.cfg
+        d = _lib.DecodeModel()
+        d.layers, d.hidden, d.intermediate = cfg.layers, cfg.hidden, cfg.intermediate
+        d.heads, d.kv_heads, d.head_dim = cfg.heads, cfg.kv_heads, cfg.head_dim
+        d.vocab, d.max_seq, d.eps = cfg.vocab, cfg.max_seq, cfg.rms_eps
+        for name in ("qkv", "o", "gu", "down"):
+            setattr(d, f"{name}_packed", self.w4[name][0].data_ptr())
+            setattr(d, f"{name}_scales", self.w4[name][1].data_ptr())
+        d.qkv_bias, d.in_norm = self.b_qkv.data_ptr(), self.in_norms.data_ptr()
+        d.post_norm, d.final_norm = self.post_norms.data_ptr(), self.final_norm.data_ptr()
+        d.embed, d.cos_table, d.sin_table = (self.embed.data_ptr(), self.cos.data_ptr(),
+                                             self.sin.data_ptr())
+        d.k_cache, d.v_cache = self.k_cache.data_ptr(), self.v_cache.data_ptr()
+        d.prompt, d.prompt_len = self.prompt.data_ptr(), self.prompt_len.data_ptr()
+        d.token, d.pos, d.logits = (self.token.data_ptr(), self.pos.data_ptr(),
+                                    self.logits.data_ptr())
+        lib = _lib.load()
+        n = ctypes.c_size_t(0)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.w4_decode_step_scratch_bytes(ctypes.byref(d), ctypes.byref(n)),
+                       "w4_decode_step_scratch_bytes")
+        self._desc = d
+        self.scratch = torch.zeros((int(n.value),), dtype=torch.uint8, device=self.device)
 
     # ---------------------------------------------------------------- ops
     def rmsnorm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -166,10 +224,18 @@ class W4DecodeModel:
     def forward_token(self) -> None:
         """One decode step on the device state (capturable: no host syncs)."""
         with torch.cuda.nvtx.range("w4_decode_step"):  # lets a profiler select one step
-            if self.fused:
+            if self.mode == "mega":
+                self._forward_mega()
+            elif self.mode == "fused":
                 self._forward_fused()
             else:
                 self._forward_torch()
+
+    def _forward_mega(self) -> None:
+        """The step as one cooperative launch of libw4b200.so (w4_decode_step)."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.load().w4_decode_step(ctypes.byref(self._desc), self.scratch.data_ptr(),
+                                              self.scratch.numel(), stream), "w4_decode_step")
 
     def _gemv_cfgs(self) -> dict:
         if self._cfgs is None:
@@ -247,7 +313,12 @@ class W4DecodeModel:
     # ---------------------------------------------------------------- driver
     def tune(self) -> None:
         """Tunes (or loads) every GEMV tile; must run before capture."""
-        self._gemv_cfgs()
+        if self.mode != "mega":
+            self._gemv_cfgs()
+
+    def launches_per_step(self) -> int:
+        """Kernels of libw4b200.so one step launches."""
+        return 1 if self.mode == "mega" else 2 + 5 * self.cfg.layers
 
     def set_prompt(self, ids: torch.Tensor) -> None:
         n = ids.numel()

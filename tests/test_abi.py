@@ -61,6 +61,30 @@ def test_validation_happens_before_any_cuda_call():
     assert st == _lib.W4_ERR_INVALID_ARG
 
 
+def test_decode_step_validation_happens_before_any_cuda_call():
+    import ctypes
+
+    lib = _lib.load()
+    n = ctypes.c_size_t(0)
+    assert lib.w4_decode_step(None, None, 0, None) == _lib.W4_ERR_INVALID_ARG
+    assert lib.w4_decode_step_scratch_bytes(None, ctypes.byref(n)) == _lib.W4_ERR_INVALID_ARG
+    d = _lib.DecodeModel(layers=2, hidden=512, intermediate=1024, heads=4, kv_heads=2,
+                         head_dim=128, vocab=1000, max_seq=64, eps=1e-6)
+    for name, _ in _lib.DecodeModel._fields_[9:]:
+        setattr(d, name, 1 << 20)  # fake, aligned device addresses (never dereferenced)
+    d.logits = None
+    d.head_dim = 64
+    assert lib.w4_decode_step(ctypes.byref(d), 1 << 20, 1 << 20, None) == _lib.W4_ERR_UNSUPPORTED
+    d.head_dim = 128
+    d.heads = 3  # heads * head_dim != hidden
+    assert lib.w4_decode_step(ctypes.byref(d), 1 << 20, 1 << 20, None) == _lib.W4_ERR_INVALID_ARG
+    d.heads = 4
+    d.embed = None
+    assert lib.w4_decode_step(ctypes.byref(d), 1 << 20, 1 << 20, None) == _lib.W4_ERR_INVALID_ARG
+    d.embed = (1 << 20) + 8
+    assert lib.w4_decode_step(ctypes.byref(d), 1 << 20, 1 << 20, None) == _lib.W4_ERR_ALIGNMENT
+
+
 def test_check_maps_status_to_exceptions():
     with pytest.raises(ValueError):
         _lib.check(_lib.W4_ERR_INVALID_ARG, "x")
