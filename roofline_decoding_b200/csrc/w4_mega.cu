@@ -50,13 +50,14 @@ constexpr int kSlotScaleBytes = kGroupsPerStage * kScaleGroupBytes;  // multiple
 constexpr int kSlots = 7;
 constexpr int kMaxStagedGroups = 32;   // x staged per CTA and phase: 4096 activations
 constexpr int kMaxItems = 4;           // GEMV items per CTA and phase
+constexpr int kMaxPartSplit = 3;       // K splits of a GEMV: partial loads are issued together
 constexpr int kAttnTileM = 32;         // positions per attention tile
 constexpr int kHD = 128;               // head_dim (= K group)
 constexpr int kKPitchM = kHD + 8;      // bf16 per K row: 16-byte rows, 4-bank skew
 constexpr int kQPitchM = kHD + 4;      // floats per q row
 constexpr int kMaxGroupHeads = 8;      // q heads per KV head
 constexpr int kMaxAttnSplits = 16;
-constexpr int kWorkBytes = 40 * 1024;  // per-phase scratch (aliased by phase type)
+constexpr int kWorkBytes = 44 * 1024;  // per-phase scratch (aliased by phase type)
 constexpr int kBarCounters = 8;        // grid-barrier arrival counters, 128 B apart
 
 constexpr int kErrBarrier = 4;  // a grid barrier wait gave up
@@ -198,11 +199,21 @@ constexpr int kAttnKnOff = kAttnQOff + kMaxGroupHeads * kQPitchM * 4;   // f32 [
 constexpr int kAttnVnOff = kAttnKnOff + kHD * 4;                        // f32 [128]
 constexpr int kAttnScOff = kAttnVnOff + kHD * 4;                        // f32 [tile][G]
 constexpr int kAttnStatOff = kAttnScOff + kAttnTileM * kMaxGroupHeads * 4;  // f32 [3][G]
-constexpr int kAttnTileOff = (kGemvWorkEnd + 127) / 128 * 128;          // bf16 K [tile][pitch]
+// q|k|v partials of the KV head, [split][(G+2)*128] f32, staged by cp.async
+// before raw is formed (q_s and the rest are written only afterwards)
+constexpr int kAttnPartOff = kAttnQOff;
+constexpr int kAttnPartEnd = kAttnPartOff + kMaxPartSplit * (kMaxGroupHeads + 2) * kHD * 4;
+constexpr int kAttnTileOff =
+    ((kGemvWorkEnd > kAttnPartEnd ? kGemvWorkEnd : kAttnPartEnd) + 127) / 128 * 128;
 constexpr int kAttnVtOff = kAttnTileOff + kAttnTileM * kKPitchM * 2;    // bf16 V [tile][128]
 constexpr int kAttnEnd = kAttnVtOff + kAttnTileM * kHD * 2;
+// RMSNorm staging: the residual's partials [split][hidden] f32, by cp.async,
+// over the tile buffers (no tile is in flight while a RMSNorm stages)
+constexpr int kNormPartOff = kAttnTileOff;
+constexpr int kNormPartEnd = kNormPartOff + kMaxPartSplit * 2048 * 4;
 static_assert(kAttnStatOff + 3 * kMaxGroupHeads * 4 <= kAttnTileOff, "attention view");
-static_assert(kAttnEnd <= kWorkBytes, "work area");
+static_assert(kAttnEnd <= kWorkBytes && kNormPartEnd <= kWorkBytes, "work area");
+static_assert(kNC == 2 * kHD, "attention P.V: two threads per dimension");
 static_assert((kAttnTileOff & 15) == 0 && (kAttnVtOff & 15) == 0, "cp.async destinations");
 
 __device__ __forceinline__ void report(int* err, int code) {
@@ -257,19 +268,56 @@ __device__ __forceinline__ uint4 load_norm(const uint16_t* w, int H) {
                              : make_uint4(0u, 0u, 0u, 0u);
 }
 
-// h_new (one bf16 row of `hidden`) from the phase's source, its RMSNorm with
-// the weight slice wv written to xsrc (bf16), and h_new stored to `h_out` by
-// CTA 0.
+// Permutes one packed row's 8 activations into the MMA k order (x0,x4)
+// (x1,x5) (x2,x6) (x3,x7), stores it at row r of xs and returns its beta
+// share (the bf16 unpack offset 136 times the row's sum).
+__device__ __forceinline__ float put_row(uint8_t* xs, int r, uint4 v) {
+  uint4 o;
+  o.x = __byte_perm(v.x, v.z, 0x5410);
+  o.y = __byte_perm(v.x, v.z, 0x7632);
+  o.z = __byte_perm(v.y, v.w, 0x5410);
+  o.w = __byte_perm(v.y, v.w, 0x7632);
+  *reinterpret_cast<uint4*>(xs + r * 16) = o;
+  const uint32_t* oi = reinterpret_cast<const uint32_t*>(&o);
+  const float ax = bfm(oi[0] & 0xffffu), ay = bfm(oi[0] >> 16);
+  const float bx = bfm(oi[1] & 0xffffu), by = bfm(oi[1] >> 16);
+  const float cx = bfm(oi[2] & 0xffffu), cy = bfm(oi[2] >> 16);
+  const float dx = bfm(oi[3] & 0xffffu), dy = bfm(oi[3] >> 16);
+  return kBF16Offset * (((ax + ay) + (cx + cy)) + ((bx + by) + (dx + dy)));
+}
+
+// Sums the beta shares of 16 consecutive rows (16 consecutive lanes) and
+// stores the group's beta. Every lane of the warp must call it.
+__device__ __forceinline__ void put_beta(float* beta, int r, bool active, float b) {
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) b += __shfl_xor_sync(0xffffffffu, b, off);
+  if (active && (r & 15) == 0) beta[r >> 4] = b;
+}
+
+// h_new (one bf16 row of `hidden`) from the phase's source and its RMSNorm
+// with the weight slice wv. Thread t owns elements 8t..8t+7, which is packed
+// row t, so it stages groups [gk0, gk1) of x straight into xs (MMA k order,
+// with beta) and, with to_xsrc, the whole row into xsrc. CTA 0 stores h_new
+// to h_out.
 __device__ void stage_rmsnorm(const MegaParams& p, int src, int64_t tok, const uint16_t* h_in,
-                              const float* part, int split, uint4 wv, uint16_t* h_out,
-                              uint8_t* work) {
+                              const float* part, int split, uint4 wv, uint16_t* h_out, int gk0,
+                              int gk1, bool to_xsrc, uint8_t* work) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int H = p.hidden;
   uint16_t* xsrc = reinterpret_cast<uint16_t*>(work + kXsrcOff);
+  uint8_t* xs = work + kXsOff;
+  float* beta = reinterpret_cast<float*>(work + kBetaOff);
   float* misc = reinterpret_cast<float*>(work + kMiscOff);
   float hv[8];
   float ss = 0.f;
   const bool act = t < H / 8;
+  if (src != kSrcEmbed) {  // every partial of the row in flight at once (one round trip)
+    float* ps = reinterpret_cast<float*>(work + kNormPartOff);
+    for (int c = t; c < split * H / 4; c += kNC) cp_async16(ps + 4 * c, part + 4 * c);
+    cp_async_commit();
+    cp_async_wait_all();
+    consumers_sync();
+  }
   if (act) {
     if (src == kSrcEmbed) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.embed + (size_t)tok * H) + t);
@@ -282,12 +330,13 @@ __device__ void stage_rmsnorm(const MegaParams& p, int src, int64_t tok, const u
     } else {
       const uint4 v = __ldcg(reinterpret_cast<const uint4*>(h_in) + t);
       const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v);
+      const float* ps = reinterpret_cast<const float*>(work + kNormPartOff);
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int s = 0; s < split; ++s) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(part + (size_t)s * H + 8 * t));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(part + (size_t)s * H + 8 * t) + 1);
+      for (int s = 0; s < split; ++s) {  // staged in shared memory, summed in split order
+        const float4 a = *reinterpret_cast<const float4*>(ps + (size_t)s * H + 8 * t);
+        const float4 b = *reinterpret_cast<const float4*>(ps + (size_t)s * H + 8 * t + 4);
         acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
         acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
       }
@@ -316,56 +365,80 @@ __device__ void stage_rmsnorm(const MegaParams& p, int src, int64_t tok, const u
 #pragma unroll
   for (int i = 0; i < kMegaConsumerWarps; ++i) tot += misc[i];
   const float inv = rsqrtf(tot / (float)H + p.eps);
+  uint4 x = make_uint4(0u, 0u, 0u, 0u);
   if (act) {
     const uint32_t* wi = reinterpret_cast<const uint32_t*>(&wv);
-    uint4 o;
-    uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+    uint32_t* xi = reinterpret_cast<uint32_t*>(&x);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float a = rbfm(hv[2 * i] * inv) * bfm(wi[i] & 0xffffu);
       const float b = rbfm(hv[2 * i + 1] * inv) * bfm(wi[i] >> 16);
-      oi[i] = (uint32_t)to_bfm(a) | ((uint32_t)to_bfm(b) << 16);
+      xi[i] = (uint32_t)to_bfm(a) | ((uint32_t)to_bfm(b) << 16);
     }
-    reinterpret_cast<uint4*>(xsrc)[t] = o;
+    if (to_xsrc) reinterpret_cast<uint4*>(xsrc)[t] = x;
   }
-  consumers_sync();  // xsrc complete; misc free again
+  if (gk1 > gk0) {  // uniform over the CTA
+    const int r = t - gk0 * 16;  // packed row t in the staged range
+    const bool in = act && r >= 0 && r < (gk1 - gk0) * 16;
+    const float b = in ? put_row(xs, r, x) : 0.f;
+    put_beta(beta, r, in, b);
+  }
+  consumers_sync();  // xs, beta (and xsrc) complete; misc free again
 }
 
-// Merged attention output for heads [hb, he) into xsrc (absolute index), one
-// round trip: every (head, dimension) thread loads the splits' (m, l, o) and
-// merges them in split order.
-__device__ void stage_attn_merge(const MegaParams& p, int hb, int he, uint8_t* work) {
-  const int G = p.group, A = p.attn_splits;
+// Position splits in use at this position: one per attention tile of cached
+// positions, at most attn_splits (the attention and the merge both derive it
+// from pos).
+__device__ __forceinline__ int attn_splits_at(const MegaParams& p, int pos) {
+  return max(1, min(p.attn_splits, (pos + 1 + kAttnTileM - 1) / kAttnTileM));
+}
+
+// Merged attention output for heads [hb, he) into xsrc (absolute index).
+// A warp merges one (head, 64 dimensions): lanes 0..15 hold the splits'
+// running maxima, lanes 16..31 their sums; the weights are broadcast by
+// shuffles and every split's slice is read once, coalesced. Fixed order.
+__device__ void stage_attn_merge(const MegaParams& p, int hb, int he, int pos, uint8_t* work) {
+  const int G = p.group, A = attn_splits_at(p, pos);
   const int stride = G * (2 + kHD);  // floats per (kv head, split) record
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint16_t* xsrc = reinterpret_cast<uint16_t*>(work + kXsrcOff);
-  for (int idx = threadIdx.x; idx < (he - hb) * kHD; idx += kNC) {
-    const int h = hb + idx / kHD, d = idx % kHD;
+  for (int u = warp; u < (he - hb) * 2; u += kMegaConsumerWarps) {
+    const int h = hb + (u >> 1), d0 = (u & 1) * 64;
     const int kvh = h / G, i = h - kvh * G;
-    const float* rec = p.pattn + (size_t)kvh * A * stride;
-    float m[kMaxAttnSplits], l[kMaxAttnSplits], o[kMaxAttnSplits];
+    const float* rec = p.pattn + (size_t)kvh * p.attn_splits * stride;
+    const int a_ml = lane & 15;
+    float ml = (lane < 16) ? -INFINITY : 0.f;
+    if (a_ml < A) ml = __ldcg(rec + (size_t)a_ml * stride + (lane < 16 ? i : G + i));
+    float o0[kMaxAttnSplits], o1[kMaxAttnSplits];
 #pragma unroll
     for (int a = 0; a < kMaxAttnSplits; ++a) {
       if (a < A) {
-        const float* r = rec + (size_t)a * stride;
-        m[a] = __ldcg(r + i);
-        l[a] = __ldcg(r + G + i);
-        o[a] = __ldcg(r + 2 * G + i * kHD + d);
+        const float* r = rec + (size_t)a * stride + 2 * G + i * kHD + d0 + lane;
+        o0[a] = __ldcg(r);
+        o1[a] = __ldcg(r + 32);
       }
     }
-    float M = -INFINITY;
+    float M = lane < 16 ? ml : -INFINITY;
 #pragma unroll
-    for (int a = 0; a < kMaxAttnSplits; ++a)
-      if (a < A) M = fmaxf(M, m[a]);
-    float L = 0.f, O = 0.f;
+    for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    M = __shfl_sync(0xffffffffu, M, 0);
+    const float lsum = __shfl_sync(0xffffffffu, ml, (lane & 15) + 16);  // l of split lane&15
+    const float w = (lane < 16 && a_ml < A && ml != -INFINITY) ? __expf(ml - M) : 0.f;
+    float L = w * lsum;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    L = __shfl_sync(0xffffffffu, L, 0);
+    float O0 = 0.f, O1 = 0.f;
 #pragma unroll
     for (int a = 0; a < kMaxAttnSplits; ++a) {
       if (a < A) {
-        const float w = (m[a] == -INFINITY) ? 0.f : __expf(m[a] - M);
-        L = fmaf(w, l[a], L);
-        O = fmaf(w, o[a], O);
+        const float wa = __shfl_sync(0xffffffffu, w, a);
+        O0 = fmaf(wa, o0[a], O0);
+        O1 = fmaf(wa, o1[a], O1);
       }
     }
-    xsrc[h * kHD + d] = to_bfm(O / L);
+    xsrc[h * kHD + d0 + lane] = to_bfm(O0 / L);
+    xsrc[h * kHD + d0 + 32 + lane] = to_bfm(O1 / L);
   }
   consumers_sync();
 }
@@ -378,10 +451,29 @@ __device__ void stage_x(const MegaParams& p, int kind, int gk0, int gk1, uint8_t
   uint8_t* xs = work + kXsOff;
   float* beta = reinterpret_cast<float*>(work + kBetaOff);
   const int rb = gk0 * 16, nrows = (gk1 - gk0) * 16;
-  const MegaGemv& gu = p.g[2];
   const float* pgu = p.part[2];
   const int I = p.inter;
-  for (int base = 0; base < nrows; base += kNC) {  // uniform trip count
+  static_assert(kMaxStagedGroups * 16 <= 2 * kNC, "at most two staged rows per thread");
+  // gate|up runs unsplit (planned with split 1), so a row's gate and up are
+  // one partial each; both rows' loads are in flight together
+  float4 gl[2][2], ul[2][2];
+  if (kind == 1) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int r = u * kNC + t;
+      const int k = (rb + min(r, nrows - 1)) * 8;
+      if (r < nrows) {
+        gl[u][0] = __ldcg(reinterpret_cast<const float4*>(pgu + k));
+        gl[u][1] = __ldcg(reinterpret_cast<const float4*>(pgu + k) + 1);
+        ul[u][0] = __ldcg(reinterpret_cast<const float4*>(pgu + I + k));
+        ul[u][1] = __ldcg(reinterpret_cast<const float4*>(pgu + I + k) + 1);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {  // uniform trip count
+    const int base = u * kNC;
+    if (base >= nrows) break;    // uniform over the CTA
     const int r = base + t;
     const bool active = r < nrows;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -390,50 +482,21 @@ __device__ void stage_x(const MegaParams& p, int kind, int gk0, int gk1, uint8_t
       if (kind == 0) {
         v = *reinterpret_cast<const uint4*>(xsrc + k);
       } else {
-        float g[8], u[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) g[i] = u[i] = 0.f;
-        for (int s = 0; s < gu.split; ++s) {
-          const float* ps = pgu + (size_t)s * gu.N;
-          const float4 g0 = __ldcg(reinterpret_cast<const float4*>(ps + k));
-          const float4 g1 = __ldcg(reinterpret_cast<const float4*>(ps + k) + 1);
-          const float4 u0 = __ldcg(reinterpret_cast<const float4*>(ps + I + k));
-          const float4 u1 = __ldcg(reinterpret_cast<const float4*>(ps + I + k) + 1);
-          g[0] += g0.x; g[1] += g0.y; g[2] += g0.z; g[3] += g0.w;
-          g[4] += g1.x; g[5] += g1.y; g[6] += g1.z; g[7] += g1.w;
-          u[0] += u0.x; u[1] += u0.y; u[2] += u0.z; u[3] += u0.w;
-          u[4] += u1.x; u[5] += u1.y; u[6] += u1.z; u[7] += u1.w;
-        }
+        const float g[8] = {gl[u][0].x, gl[u][0].y, gl[u][0].z, gl[u][0].w,
+                            gl[u][1].x, gl[u][1].y, gl[u][1].z, gl[u][1].w};
+        const float uu[8] = {ul[u][0].x, ul[u][0].y, ul[u][0].z, ul[u][0].w,
+                             ul[u][1].x, ul[u][1].y, ul[u][1].z, ul[u][1].w};
         uint32_t* vi = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float a = swiglu(rbfm(g[2 * i]), rbfm(u[2 * i]));
-          const float b = swiglu(rbfm(g[2 * i + 1]), rbfm(u[2 * i + 1]));
+          const float a = swiglu(rbfm(g[2 * i]), rbfm(uu[2 * i]));
+          const float b = swiglu(rbfm(g[2 * i + 1]), rbfm(uu[2 * i + 1]));
           vi[i] = (uint32_t)to_bfm(a) | ((uint32_t)to_bfm(b) << 16);
         }
       }
     }
-    // MMA k order: (x0,x4) (x1,x5) (x2,x6) (x3,x7)
-    uint4 o;
-    o.x = __byte_perm(v.x, v.z, 0x5410);
-    o.y = __byte_perm(v.x, v.z, 0x7632);
-    o.z = __byte_perm(v.y, v.w, 0x5410);
-    o.w = __byte_perm(v.y, v.w, 0x7632);
-    float bsum = 0.f;
-    if (active) {
-      *reinterpret_cast<uint4*>(xs + r * 16) = o;
-      const uint32_t* oi = reinterpret_cast<const uint32_t*>(&o);
-      const float ax = bfm(oi[0] & 0xffffu), ay = bfm(oi[0] >> 16);
-      const float bx = bfm(oi[1] & 0xffffu), by = bfm(oi[1] >> 16);
-      const float cx = bfm(oi[2] & 0xffffu), cy = bfm(oi[2] >> 16);
-      const float dx = bfm(oi[3] & 0xffffu), dy = bfm(oi[3] >> 16);
-      const float lo = (ax + ay) + (cx + cy);
-      const float hi = (bx + by) + (dx + dy);
-      bsum = kBF16Offset * (lo + hi);
-    }
-#pragma unroll
-    for (int off = 8; off > 0; off >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
-    if (active && (r & 15) == 0) beta[r >> 4] = bsum;
+    const float b = active ? put_row(xs, r, v) : 0.f;
+    put_beta(beta, r, active, b);
   }
   consumers_sync();
 }
@@ -486,43 +549,72 @@ __device__ void gemv_items(const MegaParams& p, int gi, const MegaSmem& sm, Ring
       const bool live = !aborted(sm.abort_flag);
       const uint32_t wslot = smem_u32(sm.w) + ring.slot * kSlotBytes;
       const uint32_t sslot = smem_u32(sm.sc) + ring.slot * kSlotScaleBytes;
-      // first group of this stage for this warp under the round-robin deal
+      // first group of this stage for this warp under the round-robin deal;
+      // a warp's two groups of a stage (q, q + 8) run interleaved
       for (int q = (warp - task % kMegaConsumerWarps + kMegaConsumerWarps) % kMegaConsumerWarps;
-           q < n && live; q += kMegaConsumerWarps) {
-        const int gl = sg + q - gx0;  // group index in the staged x
-        const float nb = -beta[gl];
-        float c[2][4];
+           q < n && live; q += 2 * kMegaConsumerWarps) {
+        const bool two = q + kMegaConsumerWarps < n;
+        const int qb = two ? q + kMegaConsumerWarps : q;  // single: the second lane set is a copy
+        const int ga = sg + q - gx0, gb = sg + qb - gx0;  // group indices in the staged x
+        float ca[2][4], cb[2][4];
+        {
+          const float na = -beta[ga], nb = -beta[gb];
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+          for (int z = 0; z < 2; ++z)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) c[a][i] = nb;
-        const uint32_t wbox = wslot + q * kGroupBytes;
+            for (int i = 0; i < 4; ++i) {
+              ca[z][i] = na;
+              cb[z][i] = nb;
+            }
+        }
+        const uint32_t wa_box = wslot + q * kGroupBytes, wb_box = wslot + qb * kGroupBytes;
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int row = 8 * o + 2 * t + e;
-            const uint4 wv = lds128(wbox + row * 128 + ((g ^ (2 * t + e)) << 4));
-            const uint4 xb = lds128(xs_base + (gl * 16 + 8 * o + e) * 16);
-            uint32_t ha[4], hb[4];
-            unpack_nibbles<true>(wv.x, ha);
-            unpack_nibbles<true>(wv.y, hb);
-            mma_16816<true>(c[0], ha[0], hb[0], ha[1], hb[1], xb.x, xb.y);
-            mma_16816<true>(c[0], ha[2], hb[2], ha[3], hb[3], xb.z, xb.w);
-            unpack_nibbles<true>(wv.z, ha);
-            unpack_nibbles<true>(wv.w, hb);
-            mma_16816<true>(c[1], ha[0], hb[0], ha[1], hb[1], xb.x, xb.y);
-            mma_16816<true>(c[1], ha[2], hb[2], ha[3], hb[3], xb.z, xb.w);
+            const uint32_t woff = row * 128 + ((g ^ (2 * t + e)) << 4);
+            const uint4 wa = lds128(wa_box + woff);
+            const uint4 wb = lds128(wb_box + woff);
+            const uint4 xa = lds128(xs_base + (ga * 16 + 8 * o + e) * 16);
+            const uint4 xb = lds128(xs_base + (gb * 16 + 8 * o + e) * 16);
+            uint32_t h0[4], h1[4], k0[4], k1[4];
+            unpack_nibbles<true>(wa.x, h0);
+            unpack_nibbles<true>(wa.y, h1);
+            unpack_nibbles<true>(wb.x, k0);
+            unpack_nibbles<true>(wb.y, k1);
+            mma_16816<true>(ca[0], h0[0], h1[0], h0[1], h1[1], xa.x, xa.y);
+            mma_16816<true>(cb[0], k0[0], k1[0], k0[1], k1[1], xb.x, xb.y);
+            mma_16816<true>(ca[0], h0[2], h1[2], h0[3], h1[3], xa.z, xa.w);
+            mma_16816<true>(cb[0], k0[2], k1[2], k0[3], k1[3], xb.z, xb.w);
+            unpack_nibbles<true>(wa.z, h0);
+            unpack_nibbles<true>(wa.w, h1);
+            unpack_nibbles<true>(wb.z, k0);
+            unpack_nibbles<true>(wb.w, k1);
+            mma_16816<true>(ca[1], h0[0], h1[0], h0[1], h1[1], xa.x, xa.y);
+            mma_16816<true>(cb[1], k0[0], k1[0], k0[1], k1[1], xb.x, xb.y);
+            mma_16816<true>(ca[1], h0[2], h1[2], h0[3], h1[3], xa.z, xa.w);
+            mma_16816<true>(cb[1], k0[2], k1[2], k0[3], k1[3], xb.z, xb.w);
           }
         }
-        const uint32_t sc = sslot + q * kScaleGroupBytes + 4 * g * 2;
-        const uint32_t s01 = lds32(sc), s23 = lds32(sc + 4);
-        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&s01));
-        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
-        acc[0] = fmaf(f01.x, c[0][0], acc[0]);
-        acc[1] = fmaf(f01.y, c[0][2], acc[1]);
-        acc[2] = fmaf(f23.x, c[1][0], acc[2]);
-        acc[3] = fmaf(f23.y, c[1][2], acc[3]);
+        const uint32_t sa = sslot + q * kScaleGroupBytes + 4 * g * 2;
+        const uint32_t sb = sslot + qb * kScaleGroupBytes + 4 * g * 2;
+        const uint32_t a01 = lds32(sa), a23 = lds32(sa + 4);
+        const float2 fa01 = __half22float2(*reinterpret_cast<const __half2*>(&a01));
+        const float2 fa23 = __half22float2(*reinterpret_cast<const __half2*>(&a23));
+        acc[0] = fmaf(fa01.x, ca[0][0], acc[0]);
+        acc[1] = fmaf(fa01.y, ca[0][2], acc[1]);
+        acc[2] = fmaf(fa23.x, ca[1][0], acc[2]);
+        acc[3] = fmaf(fa23.y, ca[1][2], acc[3]);
+        if (two) {
+          const uint32_t b01 = lds32(sb), b23 = lds32(sb + 4);
+          const float2 fb01 = __half22float2(*reinterpret_cast<const __half2*>(&b01));
+          const float2 fb23 = __half22float2(*reinterpret_cast<const __half2*>(&b23));
+          acc[0] = fmaf(fb01.x, cb[0][0], acc[0]);
+          acc[1] = fmaf(fb01.y, cb[0][2], acc[1]);
+          acc[2] = fmaf(fb23.x, cb[1][0], acc[2]);
+          acc[3] = fmaf(fb23.y, cb[1][2], acc[3]);
+        }
       }
       task += n;
       __syncwarp();
@@ -606,7 +698,7 @@ __device__ void load_kv_tile(const MegaParams& p, size_t cache_head, int t0, int
 
 __device__ AttnPre attention_prefetch(const MegaParams& p, int l, int pos, uint8_t* work) {
   AttnPre pre;
-  const int A = p.attn_splits;
+  const int A = attn_splits_at(p, pos);
   pre.kvh = blockIdx.x / A;
   pre.a = blockIdx.x - pre.kvh * A;
   const int P = pos + 1;
@@ -635,7 +727,7 @@ __device__ AttnPre attention_prefetch(const MegaParams& p, int l, int pos, uint8
 
 __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnPre& pre,
                                 uint8_t* work) {
-  const int G = p.group, A = p.attn_splits;
+  const int G = p.group, A = p.attn_splits;  // record stride: the planned split count
   const int kvh = pre.kvh, a = pre.a, j0 = pre.j0, j1 = pre.j1;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   uint16_t* raw = reinterpret_cast<uint16_t*>(work + kAttnRawOff);
@@ -652,14 +744,24 @@ __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnP
   const MegaGemv& gq = p.g[0];
   const float* pq = p.part[0];
   // q heads, k and v of this KV head: bf16(sum of partials + bias)
+  {  // every split's q heads, k and v of this KV head in flight at once (cp.async)
+    float* ps = reinterpret_cast<float*>(work + kAttnPartOff);
+    const int per = (G + 2) * kHD;  // floats per split; 16-byte chunks never cross a head
+    for (int c = t; c < gq.split * per / 4; c += kNC) {
+      const int s = (4 * c) / per, i = 4 * c - s * per;
+      cp_async16(ps + 4 * c, pq + (size_t)s * nq + attn_elem(p, kvh, i));
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    consumers_sync();
 #pragma unroll
-  for (int j = 0; j < 5; ++j) {
-    const int i = t + j * kNC;
-    if (i < (G + 2) * kHD) {
-      const int n = attn_elem(p, kvh, i);
-      float v = 0.f;
-      for (int s = 0; s < gq.split; ++s) v += __ldcg(pq + (size_t)s * nq + n);
-      raw[i] = to_bfm(v + pre.bias[j]);
+    for (int j = 0; j < 5; ++j) {
+      const int i = t + j * kNC;
+      if (i < per) {
+        float v = 0.f;
+        for (int s = 0; s < gq.split; ++s) v += ps[s * per + i];
+        raw[i] = to_bfm(v + pre.bias[j]);
+      }
     }
   }
   const size_t cache_head = ((size_t)l * p.kv_heads + kvh) * p.max_seq;
@@ -679,9 +781,10 @@ __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnP
       p.v_cache[(cache_head + pos) * kHD + t] = to_bfm(vv);
     }
   }
-  float o[kMaxGroupHeads];
+  const int dd = t & (kHD - 1), hh = t >> 7;  // P.V: dimension and head parity
+  float o[kMaxGroupHeads / 2];
 #pragma unroll
-  for (int h = 0; h < kMaxGroupHeads; ++h) o[h] = 0.f;
+  for (int j = 0; j < kMaxGroupHeads / 2; ++j) o[j] = 0.f;
   for (int t0 = j0; t0 < j1; t0 += kAttnTileM) {
     const int t1 = min(j1, t0 + kAttnTileM);
     const int n = t1 - t0;
@@ -691,22 +794,37 @@ __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnP
     }
     cp_async_wait_all();
     consumers_sync();  // tile, q_s and kn_s visible to every consumer
-    for (int pi = t; pi < n * G; pi += kNC) {  // scores
-      const int jl = pi / G, h = pi - jl * G;
-      const float* qh = q_s + h * kQPitchM;
+    // scores: four consecutive lanes share one (position, head) dot product,
+    // lane part p taking the words 4w + p, then a fixed two-step shuffle sum
+    for (int base = 0; base < n * G * 4; base += kNC) {  // uniform trip count
+      const int i = base + t;
+      const int pi = i >> 2, part = i & 3;
+      const bool act = pi < n * G;
       float d = 0.f;
-      if (t0 + jl == pos) {
-        for (int e = 0; e < kHD; ++e) d = fmaf(qh[e], kn_s[e], d);
-      } else {
-        const uint32_t* kw = reinterpret_cast<const uint32_t*>(kt_s + jl * kKPitchM);
-#pragma unroll 8
-        for (int e = 0; e < kHD / 2; ++e) {
-          const uint32_t kk = kw[e];
-          d = fmaf(qh[2 * e], bfm(kk & 0xffffu), d);
-          d = fmaf(qh[2 * e + 1], bfm(kk >> 16), d);
+      if (act) {
+        const int jl = pi / G, h = pi - jl * G;
+        const float* qh = q_s + h * kQPitchM;
+        if (t0 + jl == pos) {
+#pragma unroll 4
+          for (int w = 0; w < kHD / 8; ++w) {
+            const int e = 2 * (4 * w + part);
+            d = fmaf(qh[e], kn_s[e], d);
+            d = fmaf(qh[e + 1], kn_s[e + 1], d);
+          }
+        } else {
+          const uint32_t* kw = reinterpret_cast<const uint32_t*>(kt_s + jl * kKPitchM);
+#pragma unroll 4
+          for (int w = 0; w < kHD / 8; ++w) {
+            const uint32_t kk = kw[4 * w + part];
+            const int e = 2 * (4 * w + part);
+            d = fmaf(qh[e], bfm(kk & 0xffffu), d);
+            d = fmaf(qh[e + 1], bfm(kk >> 16), d);
+          }
         }
       }
-      sc_s[pi] = d * p.scale;
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      if (act && part == 0) sc_s[pi] = d * p.scale;
     }
     consumers_sync();
     for (int h = warp; h < G; h += kMegaConsumerWarps) {  // online softmax per head
@@ -732,15 +850,15 @@ __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnP
       }
     }
     consumers_sync();
-    if (t < kHD) {
+    {  // P.V: thread t owns dimension t & 127 of the heads h = (t >> 7) + 2j
 #pragma unroll
-      for (int h = 0; h < kMaxGroupHeads; ++h)
-        if (h < G) o[h] *= ha_s[h];
-      for (int jl = 0; jl < n; ++jl) {  // P.V, thread t owns dimension t
-        const float vj = (t0 + jl == pos) ? vn_s[t] : bfm(vt_s[jl * kHD + t]);
+      for (int j = 0; j < kMaxGroupHeads / 2; ++j)
+        if (hh + 2 * j < G) o[j] *= ha_s[hh + 2 * j];
+      for (int jl = 0; jl < n; ++jl) {
+        const float vj = (t0 + jl == pos) ? vn_s[dd] : bfm(vt_s[jl * kHD + dd]);
 #pragma unroll
-        for (int h = 0; h < kMaxGroupHeads; ++h)
-          if (h < G) o[h] = fmaf(sc_s[jl * G + h], vj, o[h]);
+        for (int j = 0; j < kMaxGroupHeads / 2; ++j)
+          if (hh + 2 * j < G) o[j] = fmaf(sc_s[jl * G + hh + 2 * j], vj, o[j]);
       }
     }
   }
@@ -752,11 +870,9 @@ __device__ void attention_phase(const MegaParams& p, int l, int pos, const AttnP
     rec[t] = hm_s[t];
     rec[G + t] = hl_s[t];
   }
-  if (t < kHD) {
 #pragma unroll
-    for (int h = 0; h < kMaxGroupHeads; ++h)
-      if (h < G) rec[2 * G + h * kHD + t] = o[h];
-  }
+  for (int j = 0; j < kMaxGroupHeads / 2; ++j)
+    if (hh + 2 * j < G) rec[2 * G + (hh + 2 * j) * kHD + dd] = o[j];
 }
 
 // ----------------------------------------------------------------- lm_head
@@ -937,23 +1053,23 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
   unsigned phases = 0;  // grid barriers passed
   bool ok = true;
   const int H = p.hidden;
-  const bool attn_cta = (int)blockIdx.x < p.kv_heads * p.attn_splits;
+  const bool attn_cta = (int)blockIdx.x < p.kv_heads * attn_splits_at(p, pos);
   uint4 wv = load_norm(p.in_norm, H);  // the next RMSNorm's weight slice
   for (int l = 0; l < p.layers; ++l) {
     int gk0 = 0, gk1 = 0;
     // ---- q|k|v: x = rmsnorm(h), h = embedding row or h1 + down partials
     {
       const bool mine = item_range(p.g[0], &gk0, &gk1);
+      if (!mine) gk0 = gk1 = 0;
       if (mine || blockIdx.x == 0) {
         if (l == 0)
-          stage_rmsnorm(p, kSrcEmbed, tok, nullptr, nullptr, 0, wv, p.h0, sm.work);
+          stage_rmsnorm(p, kSrcEmbed, tok, nullptr, nullptr, 0, wv, p.h0, gk0, gk1, false,
+                        sm.work);
         else
-          stage_rmsnorm(p, kSrcH1Down, tok, p.h1, p.part[3], p.g[3].split, wv, p.h0, sm.work);
+          stage_rmsnorm(p, kSrcH1Down, tok, p.h1, p.part[3], p.g[3].split, wv, p.h0, gk0, gk1,
+                        false, sm.work);
       }
-      if (mine) {
-        stage_x(p, 0, gk0, gk1, sm.work);
-        gemv_items(p, 0, sm, ring, gk0);
-      }
+      if (mine) gemv_items(p, 0, sm, ring, gk0);
     }
     grid_arrive(p, sm.abort_flag);
     AttnPre pre{};
@@ -965,7 +1081,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
     if (!(ok = grid_wait(p, ++phases, sm.abort_flag))) break;
     // ---- o: x = merged attention (head_dim = 128: K group g is head g)
     if (item_range(p.g[1], &gk0, &gk1)) {
-      stage_attn_merge(p, gk0, gk1, sm.work);
+      stage_attn_merge(p, gk0, gk1, pos, sm.work);
       stage_x(p, 0, gk0, gk1, sm.work);
       gemv_items(p, 1, sm, ring, gk0);
     }
@@ -975,12 +1091,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
     // ---- gate|up: x = rmsnorm(h1), h1 = h0 + o partials
     {
       const bool mine = item_range(p.g[2], &gk0, &gk1);
+      if (!mine) gk0 = gk1 = 0;
       if (mine || blockIdx.x == 0)
-        stage_rmsnorm(p, kSrcH0O, tok, p.h0, p.part[1], p.g[1].split, wv, p.h1, sm.work);
-      if (mine) {
-        stage_x(p, 0, gk0, gk1, sm.work);
-        gemv_items(p, 2, sm, ring, gk0);
-      }
+        stage_rmsnorm(p, kSrcH0O, tok, p.h0, p.part[1], p.g[1].split, wv, p.h1, gk0, gk1, false,
+                      sm.work);
+      if (mine) gemv_items(p, 2, sm, ring, gk0);
     }
     grid_arrive(p, sm.abort_flag);
     if (!(ok = grid_wait(p, ++phases, sm.abort_flag))) break;
@@ -997,7 +1112,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
   unsigned long long best = 0;
   if (ok) {
     // ---- lm_head: x = rmsnorm(h1 + down partials) with the final norm
-    stage_rmsnorm(p, kSrcH1Down, tok, p.h1, p.part[3], p.g[3].split, wv, nullptr, sm.work);
+    stage_rmsnorm(p, kSrcH1Down, tok, p.h1, p.part[3], p.g[3].split, wv, nullptr, 0, 0, true,
+                  sm.work);
     switch (H / 256) {
       case 1: lm_phase<1>(p, sm, ring, &best); break;
       case 2: lm_phase<2>(p, sm, ring, &best); break;
@@ -1046,7 +1162,7 @@ MegaGemv plan_gemv(int N, int K, int ctas) {
   G.groups = K / 128;
   G.strips = N / 32;
   int split = 1;
-  if (G.strips < ctas) split = std::min(std::min(G.groups, ctas / G.strips), 16);
+  if (G.strips < ctas) split = std::min(std::min(G.groups, ctas / G.strips), kMaxPartSplit);
   split = std::max(split, (G.groups + kMaxStagedGroups - 1) / kMaxStagedGroups);  // x fits
   G.gps = (G.groups + split - 1) / split;
   G.split = (G.groups + G.gps - 1) / G.gps;  // no empty split
@@ -1062,11 +1178,19 @@ bool plan_layout(const w4_decode_model& m, int ctas, MegaLayout* L) {
   L->g[0] = plan_gemv(nq, m.hidden, ctas);
   L->g[1] = plan_gemv(m.hidden, m.hidden, ctas);
   L->g[2] = plan_gemv(2 * m.intermediate, m.hidden, ctas);
+  if (L->g[2].split != 1) {  // the SwiGLU staging reads one gate|up partial
+    MegaGemv& G = L->g[2];
+    G.split = 1;
+    G.gps = G.groups;
+    G.items = G.strips;
+    G.bg = std::min(kGroupsPerStage, G.gps);
+  }
   L->g[3] = plan_gemv(m.hidden, m.intermediate, ctas);
   for (int i = 0; i < 4; ++i) {
     if (L->g[i].split > 1 && L->g[i].items > ctas) return false;  // one item, one K range
     if (L->g[i].items > kMaxItems * ctas) return false;           // per-CTA accumulators
     if (L->g[i].gps > kMaxStagedGroups) return false;
+    if (L->g[i].split > kMaxPartSplit) return false;
   }
   L->attn_splits = std::max(1, std::min(16, ctas / m.kv_heads));
   size_t off = 2048;  // barrier counters @0 (128 B apart), done @1024, best @1152
