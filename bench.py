@@ -333,8 +333,23 @@ def run_gemv_workload(args, rank, world, local):
             for (M, K, N, dt), n in zip(cases, n_loc)]
     n_launch = len(cases)
     stream = torch.cuda.Stream(device)
+    peers = None
+    if sharded and args.gather == "peer":
+        from roofline_decoding_b200._lib import GemvConfig
+        from roofline_decoding_b200.sharded import PeerGroup
+
+        peers = PeerGroup(device=device)
+        for i, (M, K, N, dt) in enumerate(cases):
+            peers.output(f"case{i}", M, N, torch.float16)
 
     def launch_all(si, pdl, ev=None, gather=True):
+        if peers is not None and gather:  # one kernel per GEMV: compute + NVLink gather
+            for i, (M, K, N, dt) in enumerate(cases):
+                p, s = pool[si][i]
+                c = cfgs[i]
+                c = GemvConfig(c.strips, c.row_groups, c.stages, c.split, 1 if pdl else 0)
+                peers.gemv(xs[i], p, s, f"case{i}", N, rank * n_loc[i], config=c)
+            return
         for i in range(n_launch):
             p, s = pool[si][i]
             Kn.w4_matmul(xs[i], p, s, out=ys[i], config=cfgs[i], pdl=pdl)
@@ -412,8 +427,10 @@ def run_gemv_workload(args, rank, world, local):
     dom_us = mean_k[dom] * 1e3
     achieved = local_bytes[dom] / (dom_us * 1e-6) / 1e9
 
+    if peers is not None:
+        peers.sync_epoch()  # graph replays advanced the device epoch
     e2e = run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered,
-                  n_loc)
+                  n_loc, peers)
     clk = clocks.summary()
     if rank == 0:
         cpu = None
@@ -430,8 +447,10 @@ def run_gemv_workload(args, rank, world, local):
             "dtype": "w4a16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) weights packed to int4, N(0,1) activations)",
             "config": {"workload": wl["desc"], "global_batch": 1 if sharded else world,
-                       "parallelism": (f"column-parallel{world} + NCCL all-gather" if sharded
-                                       else f"replicas{world}"),
+                       "parallelism": ((f"column-parallel{world} + all-gather fused into the "
+                                        "GEMV epilogue (NVLink peer stores)" if peers is not None
+                                        else f"column-parallel{world} + NCCL all-gather")
+                                       if sharded else f"replicas{world}"),
                        "l2": (f"rotating packed-weight pool of {slots} step copies "
                               f"({slots * step_bytes / 2**20:.0f} MiB >= 3x L2 "
                               f"{l2 / 2**20:.0f} MiB)"),
@@ -463,6 +482,8 @@ def run_gemv_workload(args, rank, world, local):
             line["gather_ms_per_step"] = round((elapsed_ms - ms_gemv) / args.steps, 4)
         print(json.dumps(line), flush=True)
     del graphs_pdl, graphs_gemv  # graphs holding NCCL calls go first
+    if peers is not None:
+        peers.close()
 
 
 def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
@@ -498,7 +519,8 @@ def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
     return best
 
 
-def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered, n_loc):
+def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered, n_loc,
+            peers=None):
     """Public-API steps: pinned x -> device, fused GEMV(s), y -> pinned host."""
     hx = [x.cpu().pin_memory() for x in xs]
     hy = [torch.empty((M * world if sharded else M, n), dtype=torch.float16).pin_memory()
@@ -509,6 +531,11 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
         for k in range(len(cases)):
             p, s = pool[i % slots][k]
             xd = hx[k].to(device, non_blocking=True)
+            if peers is not None:
+                M, K, N, dt = cases[k]
+                y = peers.gemv(xd, p, s, f"case{k}", N, peers.rank * n_loc[k], config=cfgs[k])
+                hy[k].view(-1).copy_(y.reshape(-1), non_blocking=True)
+                continue
             y = Kn.w4_matmul(xd, p, s, config=cfgs[k])
             if sharded:
                 import torch.distributed as dist
@@ -636,6 +663,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode"], default="sweep")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="large workload on N>1 GPUs: all-gather fused into the GEMV (peer "
+                         "stores over NVLink) or a separate NCCL all-gather")
     ap.add_argument("--decode-mode", choices=["mega", "fused"], default="fused",
                     help="decode workload: the step as one kernel or as 142 kernels")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -131,6 +131,56 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed,
                   const w4_fused_ops* ops, const w4_gemv_config* cfg,
                   void* stream);
 
+/* ---------------------------------------------------------------------
+ * Column-parallel GEMV with the all-gather fused into its epilogue.
+ *
+ * The reference runs on one GPU; its GEMV entry points
+ * (src/roofline/kernels.py:131-145, :250-268) are sharded here over the
+ * ranks of one node, column-parallel on N, as an NCCL all-gather after a
+ * local GEMV would be. Instead of that collective, every rank's kernel
+ * stores its slice of y straight into every rank's output buffer over
+ * NVLink (plain peer stores), and the last CTA of each rank publishes an
+ * epoch flag to every peer and waits (bounded) for all peers' flags. When
+ * the kernel completes, y is whole on every rank.
+ *
+ * Buffers come from w4_peer_alloc on each rank and are opened on the others
+ * with w4_peer_open (CUDA IPC). The output alternates between two buffers by
+ * epoch parity, so a rank that runs ahead never overwrites a y that a slower
+ * rank may still read; call k writes y[k % 2]. */
+#define W4B200_MAX_PEERS 8
+typedef struct w4_peer_out {
+  int world, rank;             /* ranks in the group, this rank */
+  int n_full;                  /* columns of the whole y */
+  int col_off;                 /* first column of this rank's slice */
+  void* y[2][W4B200_MAX_PEERS];          /* rank q's y buffers [M, n_full] by parity */
+  unsigned* flags[W4B200_MAX_PEERS];     /* rank q's flag words (world of them) */
+  unsigned* state;             /* this rank's own state words (zeroed once): epoch, done */
+} w4_peer_out;
+
+/* Bytes of the flag and state words a rank allocates for a group of `world`
+ * ranks (one region: flags first, then the state). */
+size_t w4_peer_flag_bytes(int world);
+
+/* y = x @ dequant(W_local) on this rank's columns, gathered into every
+ * rank's y[epoch % 2] (see above). N is the local column count; y_dtype the
+ * type of y. Blocks (bounded, 1 s) until every rank of the group ran the same
+ * call; a rank that never arrives sets the device error word. Returns the
+ * parity written through *parity (read after the stream completes: the
+ * epoch lives on the device, so the host passes the parity it expects). */
+int w4_gemv_allgather(const void* x, int x_dtype, const int32_t* packed,
+                      const void* scales, int y_dtype, int M, int K, int N,
+                      const w4_gemv_config* cfg, const w4_peer_out* peers,
+                      void* stream);
+
+/* Device memory another process on this node can map: cudaMalloc plus its
+ * IPC handle (W4B200_IPC_HANDLE_BYTES bytes written to handle). */
+#define W4B200_IPC_HANDLE_BYTES 64
+int w4_peer_alloc(size_t bytes, void** ptr, void* handle);
+int w4_peer_free(void* ptr);
+/* Maps a peer's allocation into this process (peer access enabled). */
+int w4_peer_open(const void* handle, void** ptr);
+int w4_peer_close(void* ptr);
+
 /* Decode-step kernels (bf16 activations), the rest of the batch-1 greedy
  * step that scripts/decode_loop.py:106-124 ran as an HF forward. All read
  * the step state (token, position) from device memory, so a whole step can

@@ -76,6 +76,17 @@ class DecodeModel(ctypes.Structure):
             "token", "pos", "logits")]
 
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class PeerOut(ctypes.Structure):
+    """w4_peer_out: where a column-parallel GEMV gathers its output."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("n_full", ctypes.c_int),
+                ("col_off", ctypes.c_int), ("y", (ctypes.c_void_p * MAX_PEERS) * 2),
+                ("flags", ctypes.c_void_p * MAX_PEERS), ("state", ctypes.c_void_p)]
+
+
 SIGNATURES = {
     "w4_version": (_c_int, []),
     "w4_status_string": (ctypes.c_char_p, [_c_int]),
@@ -108,6 +119,14 @@ SIGNATURES = {
     "w4_decode_step_scratch_bytes": (_c_int, [ctypes.POINTER(DecodeModel),
                                               ctypes.POINTER(_c_size_t)]),
     "w4_decode_step": (_c_int, [ctypes.POINTER(DecodeModel), _c_void_p, _c_size_t, _c_void_p]),
+    "w4_peer_flag_bytes": (_c_size_t, [_c_int]),
+    "w4_gemv_allgather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
+                                   _c_int, _c_int, ctypes.POINTER(GemvConfig),
+                                   ctypes.POINTER(PeerOut), _c_void_p]),
+    "w4_peer_alloc": (_c_int, [_c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "w4_peer_free": (_c_int, [_c_void_p]),
+    "w4_peer_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "w4_peer_close": (_c_int, [_c_void_p]),
     "w4_device_error": (_c_int, [_c_int, ctypes.POINTER(_c_int)]),
 }
 

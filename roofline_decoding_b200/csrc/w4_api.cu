@@ -2,6 +2,8 @@
 // include/w4b200.h): argument validation, one-off device set-up and dispatch.
 #include "w4_internal.h"
 
+#include <cstring>
+
 #include <cudaTypedefs.h>
 
 #include <cstdarg>
@@ -243,6 +245,76 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void*
   GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg,
                *ops};
   return launch_gemv(L, (cudaStream_t)stream);
+}
+
+size_t w4_peer_flag_bytes(int world) {
+  (void)world;
+  return 256;  // flag words at 0 (one per rank, <= 8), state words at 128
+}
+
+int w4_gemv_allgather(const void* x, int x_dtype, const int32_t* packed, const void* scales,
+                      int y_dtype, int M, int K, int N, const w4_gemv_config* cfg,
+                      const w4_peer_out* peers, void* stream) {
+  if (!cfg || !peers) return fail(W4_ERR_INVALID_ARG, "w4_gemv_allgather: null config or peers");
+  const w4_peer_out& po = *peers;
+  if (po.world < 1 || po.world > W4B200_MAX_PEERS || po.rank < 0 || po.rank >= po.world)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_allgather: rank %d of %d (at most %d ranks)",
+                po.rank, po.world, W4B200_MAX_PEERS);
+  if (po.col_off < 0 || po.n_full < po.col_off + N || po.col_off % 8 != 0 || po.n_full % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG,
+                "w4_gemv_allgather: columns [%d, %d) outside n_full=%d (multiples of 8)",
+                po.col_off, po.col_off + N, po.n_full);
+  if (!po.state || (reinterpret_cast<uintptr_t>(po.state) & 3))
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_allgather: state words missing");
+  for (int q = 0; q < po.world; ++q) {
+    if (!po.flags[q] || !po.y[0][q] || !po.y[1][q])
+      return fail(W4_ERR_INVALID_ARG, "w4_gemv_allgather: buffers of rank %d missing", q);
+    if (!aligned16(po.y[0][q]) || !aligned16(po.y[1][q]))
+      return fail(W4_ERR_ALIGNMENT, "w4_gemv_allgather: y buffers must be 16-byte aligned");
+  }
+  // the local y argument of the plain check: this rank's own buffer
+  int st = gemv_check(x, x_dtype, packed, scales, po.y[0][po.rank], y_dtype, M, K, N);
+  if (st != W4_OK) return st;
+  w4_fused_ops ops{};
+  GemvLaunch L{x, packed, scales, po.y[0][po.rank], x_dtype == W4_BF16, y_dtype == W4_BF16,
+               M, K, N, *cfg, ops, &po};
+  return launch_gemv(L, (cudaStream_t)stream);
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == W4B200_IPC_HANDLE_BYTES, "IPC handle size");
+
+int w4_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(W4_ERR_INVALID_ARG, "w4_peer_alloc: arguments");
+  int dev;
+  int st = current_device(&dev);
+  if (st != W4_OK) return st;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "w4_peer_alloc cudaMalloc");
+  if ((e = cudaMemset(*ptr, 0, bytes)) != cudaSuccess ||
+      (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr)) != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return cuda_fail(e, "w4_peer_alloc");
+  }
+  return W4_OK;
+}
+
+int w4_peer_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_peer_free");
+}
+
+int w4_peer_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(W4_ERR_INVALID_ARG, "w4_peer_open: arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_peer_open");
+}
+
+int w4_peer_close(void* ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_peer_close");
 }
 
 int w4_decode_embed(const void* embed, int vocab, int hidden, const int64_t* prompt,

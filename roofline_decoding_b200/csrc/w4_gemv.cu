@@ -58,6 +58,27 @@ struct GemvParams {
   const void* epi_src; // bias [N] or residual [M, N] (y's type; may alias y)
 };
 
+// Column-parallel output: this rank's slice of y goes to every rank's buffer
+// of the current parity, then a flag per rank says the slice is complete.
+struct PeerParams {
+  int world;            // 0: a plain GEMV (the fields below are unused)
+  int rank, n_full, col_off;
+  void* y[2][W4B200_MAX_PEERS];
+  unsigned* flags[W4B200_MAX_PEERS];  // rank q's flag words; word r is set by rank r
+  unsigned* state;                    // [0] epoch of the last completed call, [1] CTAs done
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int kErrPeerWait = 6;  // a peer's completion flag did not arrive in time
+
 __device__ __forceinline__ float ld_f(const void* p, size_t i, bool bf16) {
   const uint16_t v = static_cast<const uint16_t*>(p)[i];
   return bf16 ? __uint_as_float((uint32_t)v << 16) : __half2float(__ushort_as_half(v));
@@ -151,7 +172,8 @@ __device__ __forceinline__ uint4 permute_row(uint4 v) {
 template <bool kBF16, int MB, int SW, int RG>
 __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     w4_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
-                   const __grid_constant__ CUtensorMap tm_s, const GemvParams p) {
+                   const __grid_constant__ CUtensorMap tm_s, const GemvParams p,
+                   const __grid_constant__ PeerParams pp) {
   using T = TileShape<SW, RG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -171,6 +193,7 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
   float* s_red = s_inv + 16;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_red + RG * M * T::kNT);
   uint64_t* empty = full + S;
+  unsigned& s_epoch = *reinterpret_cast<unsigned*>(empty + S);  // gathered output: this call's epoch
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -245,6 +268,8 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     const int nct = T::kCW * 32;
     // x is produced by the previous kernel on the stream: wait for it.
     grid_dependency_wait();
+    // the previous call's last CTA advanced the epoch before that grid ended
+    if (pp.world > 0 && threadIdx.x == 0) s_epoch = __ldcg(pp.state) + 1u;
     const uint16_t* xg = static_cast<const uint16_t*>(p.x);
     // x row pitch: a SwiGLU prologue reads gate|up rows of 2K
     const size_t x_pitch = (p.pro == W4_PRO_SWIGLU) ? 2 * (size_t)p.K : (size_t)p.K;
@@ -503,10 +528,20 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
         // the residual add, as in the reference model's bf16 forward
         v = ld_f(p.epi_src, (size_t)m * p.N + n, p.y_bf16) + round_to(v, p.y_bf16);
       }
-      if (p.y_bf16)
+      if (pp.world > 0) {  // every rank's buffer of this parity (NVLink stores)
+        const size_t at = (size_t)m * pp.n_full + pp.col_off + n;
+        const int par = (int)(s_epoch & 1u);
+        for (int q = 0; q < pp.world; ++q) {
+          if (p.y_bf16)
+            static_cast<__nv_bfloat16*>(pp.y[par][q])[at] = __float2bfloat16_rn(v);
+          else
+            static_cast<__half*>(pp.y[par][q])[at] = __float2half_rn(v);
+        }
+      } else if (p.y_bf16) {
         static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v);
-      else
+      } else {
         static_cast<__half*>(p.y)[(size_t)m * p.N + n] = __float2half_rn(v);
+      }
     }
   };
 
@@ -527,13 +562,45 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     }
     cluster.sync();  // keep this CTA's shared memory alive for the readers
   }
+
+  if (pp.world > 0) {
+    // Gathered output: the CTA that finishes last on this rank publishes the
+    // epoch to every rank, then waits until every rank published it here.
+    // Each CTA orders its peer stores before its count at GPU scope (a
+    // cumulative release); the last CTA, having observed every count, makes
+    // all of them visible system-wide with one system-scope fence before it
+    // publishes.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned e = s_epoch;
+      if (atomicAdd(&pp.state[1], 1u) == total - 1) {
+        __threadfence_system();
+        for (int q = 0; q < pp.world; ++q) st_release_sys(pp.flags[q] + pp.rank, e);
+        const unsigned* mine = pp.flags[pp.rank];
+        for (int q = 0; q < pp.world; ++q) {
+          const unsigned long long t0 = globaltimer_ns();
+          while ((int)(ld_acquire_sys(mine + q) - e) < 0) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              report_error(p.err, kErrPeerWait);
+              break;
+            }
+          }
+        }
+        pp.state[1] = 0u;
+        pp.state[0] = e;
+        __threadfence();
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- host side
 
 namespace {
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemvParams);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemvParams, PeerParams);
 
 template <bool B, int MB, int SW, int RG>
 void* kptr() {
@@ -574,7 +641,7 @@ size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& c) {
   const size_t plane = (size_t)gps * 16 * 16 + 16;
   const size_t beta = (((size_t)M * gps + 3) & ~(size_t)3) * 4 + 16 * 4;
   return 1024 + c.stages * (stage + scale) + M * plane + beta + c.row_groups * M * nt * 4 +
-         2 * c.stages * sizeof(uint64_t);
+         2 * c.stages * sizeof(uint64_t) + 16;  // + the epoch word
 }
 
 int gemv_validate_config(int M, int K, int N, const w4_gemv_config& c, const DeviceInfo& di) {
@@ -729,7 +796,19 @@ int launch_gemv(const GemvLaunch& L, cudaStream_t stream) {
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  void* args[] = {&tm_w, &tm_s, &p};
+  PeerParams pp{};
+  if (L.peer) {
+    const w4_peer_out& po = *L.peer;
+    pp.world = po.world;
+    pp.rank = po.rank;
+    pp.n_full = po.n_full;
+    pp.col_off = po.col_off;
+    for (int b = 0; b < 2; ++b)
+      for (int q = 0; q < W4B200_MAX_PEERS; ++q) pp.y[b][q] = po.y[b][q];
+    for (int q = 0; q < W4B200_MAX_PEERS; ++q) pp.flags[q] = po.flags[q];
+    pp.state = po.state;
+  }
+  void* args[] = {&tm_w, &tm_s, &p, &pp};
   cudaError_t e = cudaLaunchKernelExC(&cfg, kfn, args);
   if (e != cudaSuccess) return cuda_fail(e, "w4_gemv launch");
   return W4_OK;

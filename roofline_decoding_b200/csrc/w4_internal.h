@@ -40,6 +40,7 @@ struct GemvLaunch {
   int M, K, N;
   w4_gemv_config cfg;
   w4_fused_ops ops;  // zero for a plain GEMV
+  const w4_peer_out* peer = nullptr;  // column-parallel: y gathered into every rank's buffer
 };
 size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& cfg);
 int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const DeviceInfo& di);
