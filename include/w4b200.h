@@ -131,6 +131,17 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed,
                   const w4_fused_ops* ops, const w4_gemv_config* cfg,
                   void* stream);
 
+/* w4_gemm: y[M, N] = x[M, K] @ dequantize_v1(packed, scales) on the
+ * tensor cores (tcgen05, fp32 accumulate) for any M - the prefill rows of
+ * W4Linear, which the reference runs as dequantize_v1 (kernels.py:77-90)
+ * into an fp16 [K, N] copy followed by an fp32 matmul
+ * (scripts/decode_loop.py:51-55). The dequantised tile stays in shared
+ * memory. fp16 x uses the reference's fp16 weights fp16((q - 8) * s); bf16 x
+ * uses bf16((q - 8) * s). K and N multiples of 128, pointers 16-byte
+ * aligned. */
+int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scales,
+            void* y, int y_dtype, int M, int K, int N, void* stream);
+
 /* ---------------------------------------------------------------------
  * Column-parallel GEMV with the all-gather fused into its epilogue.
  *

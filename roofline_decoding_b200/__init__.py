@@ -7,7 +7,7 @@ helpers of roofline/roofline.py. Compute goes through libw4b200.so's C ABI.
 """
 from .kernels import (GROUP_SIZE, _TUNE_CACHE, default_config, dequantize_v1, device_error,
                       gemv_v2, gemv_v3, pack_weights, reference_gemv, save_tuned_configs,
-                      tuned_config, w4_matmul)
+                      tuned_config, w4_gemm, w4_matmul)
 from .linear import W4Linear, swap_linears, weight_bytes_int4
 from .roofline import (ORCH_FUSION, QWEN_15B, achieved_bandwidth_percent, ceilings_table,
                        decode_ceiling, gemv_bytes, measure_copy_bandwidth_gbs)
@@ -16,7 +16,7 @@ __version__ = "1.0.0"
 __all__ = [
     "GROUP_SIZE", "_TUNE_CACHE", "default_config", "dequantize_v1", "device_error", "gemv_v2",
     "gemv_v3", "pack_weights", "reference_gemv", "save_tuned_configs", "tuned_config",
-    "w4_matmul", "W4Linear", "swap_linears", "weight_bytes_int4", "ORCH_FUSION", "QWEN_15B",
+    "w4_gemm", "w4_matmul", "W4Linear", "swap_linears", "weight_bytes_int4", "ORCH_FUSION", "QWEN_15B",
     "achieved_bandwidth_percent", "ceilings_table", "decode_ceiling", "gemv_bytes",
     "measure_copy_bandwidth_gbs",
 ]

@@ -94,6 +94,7 @@ int init_locked(int device) {
     st = gemv_init_device(di);
     if (st == W4_OK) st = decode_init_device(di);
     if (st == W4_OK) st = mega_init_device(di);
+    if (st == W4_OK) st = gemm_init_device(di);
   } while (false);
   if (prev != device) cudaSetDevice(prev);
   if (st == W4_OK) {
@@ -245,6 +246,21 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void*
   GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg,
                *ops};
   return launch_gemv(L, (cudaStream_t)stream);
+}
+
+int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scales, void* y,
+            int y_dtype, int M, int K, int N, void* stream) {
+  if (!x || !packed || !scales || !y) return fail(W4_ERR_INVALID_ARG, "w4_gemm: null pointer");
+  int st = check_dtype(x_dtype, "w4_gemm x");
+  if (st != W4_OK) return st;
+  if ((st = check_dtype(y_dtype, "w4_gemm y")) != W4_OK) return st;
+  if (M < 1 || K <= 0 || K % 128 != 0 || N <= 0 || N % 128 != 0)
+    return fail(W4_ERR_INVALID_ARG,
+                "w4_gemm: M=%d K=%d N=%d (M >= 1, K and N multiples of 128)", M, K, N);
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(scales) || !aligned16(y))
+    return fail(W4_ERR_ALIGNMENT, "w4_gemm: pointers must be 16-byte aligned");
+  return launch_gemm(x, x_dtype == W4_BF16, packed, scales, y, y_dtype == W4_BF16, M, K, N,
+                     (cudaStream_t)stream);
 }
 
 size_t w4_peer_flag_bytes(int world) {

@@ -65,6 +65,11 @@ int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const vo
                           int pdl, cudaStream_t stream);
 int decode_init_device(const DeviceInfo& di);
 
+// tcgen05 W4A16 GEMM (w4_gemm.cu).
+int gemm_init_device(const DeviceInfo& di);
+int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
+                int y_bf16, int M, int K, int N, cudaStream_t stream);
+
 // Whole-step persistent kernel (w4_mega.cu).
 int mega_init_device(const DeviceInfo& di);
 int decode_step_scratch_bytes(const w4_decode_model& m, size_t* bytes);

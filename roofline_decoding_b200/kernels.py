@@ -283,6 +283,53 @@ def gemv_v3(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, split_k
                      out_dtype=out_dtype)
 
 
+def w4_gemm(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
+            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ dequantize_v1(packed, scales) on the tensor cores for any number of rows.
+
+    The prefill path of W4Linear: the reference dequantises to an fp16 [K, N]
+    copy and runs an fp32 matmul (scripts/decode_loop.py:51-55); this kernel
+    dequantises tile by tile into shared memory and accumulates in fp32 with
+    tcgen05. x is [M, K] (or [K]) fp16 or bf16; N must be a multiple of 128.
+    """
+    K, N = _check_packed(packed, scales)
+    if N % 128:
+        raise ValueError(f"w4_gemm needs N % 128 == 0, got N={N}")
+    x2, squeeze = _prep_x_any_rows(x, K, packed.device)
+    M = x2.shape[0]
+    y_dtype = out_dtype or (x2.dtype if x2.dtype in _DTYPE_CODE else torch.float16)
+    if y_dtype not in _DTYPE_CODE:
+        raise ValueError(f"out_dtype must be float16 or bfloat16, got {y_dtype}")
+    if out is None:
+        y = torch.empty((M, N), dtype=y_dtype, device=packed.device)
+    else:
+        if out.dtype != y_dtype or out.numel() != M * N or not out.is_contiguous():
+            raise ValueError("out must be a contiguous tensor of M*N elements of out_dtype")
+        y = out
+    lib = _lib.load()
+    with torch.cuda.device(packed.device):
+        _lib.check(lib.w4_gemm(x2.data_ptr(), _DTYPE_CODE[x2.dtype], packed.contiguous().data_ptr(),
+                               scales.contiguous().data_ptr(), y.data_ptr(), _DTYPE_CODE[y_dtype],
+                               M, K, N, _stream_ptr(packed.device)), "w4_gemm")
+    if out is not None:
+        return out
+    return y[0] if squeeze else y
+
+
+def _prep_x_any_rows(x: torch.Tensor, K: int, device: torch.device) -> tuple[torch.Tensor, bool]:
+    """x as a contiguous [M, K] fp16/bf16 CUDA tensor for w4_gemm (any M)."""
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x.reshape(-1, x.shape[-1])
+    if x2.shape[1] != K:
+        raise ValueError(f"x has {x2.shape[1]} features, packed weights expect {K}")
+    if x2.dtype not in _DTYPE_CODE:
+        x2 = x2.half()
+    x2 = x2.to(device).contiguous()
+    if x2.data_ptr() % 16:
+        x2 = x2.clone()
+    return x2, squeeze
+
+
 def reference_gemv(x_fp16: torch.Tensor, w_fp16: torch.Tensor) -> torch.Tensor:
     """Dense fp32 reference (roofline/kernels.py:271-273)."""
     return (x_fp16.float() @ w_fp16.float()).to(torch.float16)

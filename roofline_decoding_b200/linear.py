@@ -15,7 +15,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .kernels import dequantize_v1, pack_weights, w4_matmul
+from .kernels import w4_gemm, dequantize_v1, pack_weights, w4_matmul
 
 FUSED_MAX_ROWS = 16
 
@@ -67,6 +67,8 @@ class W4Linear(nn.Module):
             flat = flat.to(out_dtype)
         if flat.shape[0] <= FUSED_MAX_ROWS:
             out = w4_matmul(flat, self.packed, self.scales, out_dtype=out_dtype)
+        elif self.out_features % 128 == 0:  # prefill rows: tcgen05 GEMM, weights never in HBM
+            out = w4_gemm(flat, self.packed, self.scales, out_dtype=out_dtype)
         else:
             w = dequantize_v1(self.packed, self.scales, out_dtype=out_dtype)
             out = (flat.float() @ w.float()).to(out_dtype)
