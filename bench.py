@@ -568,6 +568,164 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
 
 # ---------------------------------------------------------------- decode workload
 
+PREFILL_CASES = [(2048, 4096, 14336), (2048, 1536, 8960), (2048, 8960, 1536)]
+
+
+def run_prefill(args, rank, world, local):
+    """tcgen05 W4A16 GEMM for prefill rows (W4Linear above 16 rows), TFLOP/s."""
+    import torch
+
+    from roofline_decoding_b200 import kernels as Kn
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) \
+        if (REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    peak_kind = "measured" if peaks else "fallback"
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    one = []
+    for i, (M, K, N) in enumerate(PREFILL_CASES):
+        g = torch.Generator(device=device).manual_seed(100 + i + 1000 * rank)
+        w = (torch.randn((K, N), generator=g, device=device) * 0.02).half()
+        packed, scales = Kn.pack_weights(w)
+        del w
+        x = torch.randn((M, K), generator=g, device=device).half()
+        one.append((x, packed, scales))
+    step_bytes = sum(x.numel() * 2 + p.numel() * 4 + s.numel() * 2 + M * N * 2
+                     for (x, p, s), (M, K, N) in zip(one, PREFILL_CASES))
+    slots = max(2, -(-3 * l2 // step_bytes))  # every launch reads cold operands
+    pool = [one] + [[(x.clone(), p.clone(), s.clone()) for x, p, s in one]
+                    for _ in range(slots - 1)]
+    ys = [torch.empty((M, N), dtype=torch.float16, device=device) for M, K, N in PREFILL_CASES]
+    stream = torch.cuda.Stream(device)
+    flops = [2.0 * M * K * N for M, K, N in PREFILL_CASES]
+
+    def launch(si):
+        for i, (x, p, s) in enumerate(pool[si]):
+            Kn.w4_gemm(x, p, s, out=ys[i])
+
+    with torch.cuda.stream(stream):
+        for si in range(slots):
+            launch(si)
+    stream.synchronize()
+    graphs = []
+    for si in range(slots):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                launch(si)
+        graphs.append(g)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % slots].replay()
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for i in range(args.steps):
+                graphs[(args.warmup + i) % slots].replay()
+            b.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks([a.elapsed_time(b)], world)[0]
+        # per case: graphs of that GEMM alone over the rotation
+        per = []
+        for i in range(len(PREFILL_CASES)):
+            gs = []
+            for si in range(slots):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(g, stream=stream):
+                        for _ in range(4):
+                            x, p, s = pool[si][i]
+                            Kn.w4_gemm(x, p, s, out=ys[i])
+                gs.append(g)
+            with torch.cuda.stream(stream):
+                for g in gs:
+                    g.replay()
+                c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c.record(stream)
+                for r in range(20):
+                    gs[r % slots].replay()
+                d.record(stream)
+            d.synchronize()
+            per.append(c.elapsed_time(d) / 80)
+            del gs
+    per = max_over_ranks(per, world)
+    # dense comparisons on the same shapes: the reference's path (fp16 copy of
+    # the weights by dequantize_v1, then an fp32 matmul) and fp16 cuBLAS on
+    # that copy
+    ref_ms, cublas_ms = [], []
+    for (x, p, s), (M, K, N) in zip(one, PREFILL_CASES):
+        for kind in ("ref", "cublas"):
+            def f():
+                wd = Kn.dequantize_v1(p, s)
+                return (x.float() @ wd.float()).half() if kind == "ref" else x @ wd
+            for _ in range(2):
+                f()
+            torch.cuda.synchronize()
+            c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c.record()
+            for _ in range(5):
+                f()
+            d.record()
+            d.synchronize()
+            (ref_ms if kind == "ref" else cublas_ms).append(c.elapsed_time(d) / 5)
+    # e2e: x from pinned host memory, y back to pinned host memory, per GEMM
+    hx = [x.cpu().pin_memory() for x, _, _ in one]
+    hy = [torch.empty((M, N), dtype=torch.float16).pin_memory() for M, K, N in PREFILL_CASES]
+    e_steps = max(3, args.steps // 10)
+    torch.cuda.synchronize()
+    c, d = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c.record()
+    for _ in range(e_steps):
+        for i, (x, p, s) in enumerate(one):
+            y = Kn.w4_gemm(hx[i].to(device, non_blocking=True), p, s)
+            hy[i].copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    d.record()
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks([c.elapsed_time(d)], world)[0]
+    clk = clocks.summary()
+    if rank != 0:
+        return
+    dom = max(range(len(per)), key=lambda i: per[i])
+    tot_flops = sum(flops)
+    line = {
+        "metric": "W4A16 prefill GEMM TFLOP/s (tcgen05, M=2048 tokens)",
+        "value": round(tot_flops * world * args.steps / (ms / 1e3) / 1e12, 2),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 x fp16 (dequantised int4), fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights packed to int4, N(0,1) activations)",
+        "config": {"workload": "W4A16 GEMM M=2048: 2048x4096x14336, 2048x1536x8960, 2048x8960x1536",
+                   "parallelism": f"replicas{world}",
+                   "l2": f"rotating operand pool of {slots} copies ({slots * step_bytes / 2**20:.0f} MiB >= 3x L2)"},
+        "gpu_launches": len(PREFILL_CASES) * args.steps,
+        "roofline": {"bound": "tensor",
+                     "kernel": "w4_gemm_kernel M=%d K=%d N=%d" % PREFILL_CASES[dom],
+                     "achieved": round(flops[dom] / (per[dom] / 1e3) / 1e12, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(flops[dom] / (per[dom] / 1e3) / 1e12 / peak, 4),
+                     "peak_kind": peak_kind + " bf16 cuBLAS burst", "traffic": None,
+                     "mean_launch_us": round(per[dom] * 1e3, 2)},
+        "per_case": [{"M": M, "K": K, "N": N, "us": round(t * 1e3, 2),
+                      "TFLOPs": round(f / (t / 1e3) / 1e12, 1),
+                      "dense_fp16_cublas_us": round(cb * 1e3, 2),
+                      "reference_path_us": round(rf * 1e3, 2)}
+                     for (M, K, N), t, f, cb, rf in zip(PREFILL_CASES, per, flops, cublas_ms, ref_ms)],
+        "e2e": {"value": round(tot_flops * world * e_steps / (e_ms / 1e3) / 1e12, 2),
+                "unit": "TFLOP/s",
+                "h2d_bytes_per_step": sum(h.numel() * 2 for h in hx),
+                "d2h_bytes_per_step": sum(h.numel() * 2 for h in hy),
+                "path": "roofline_decoding_b200.w4_gemm per GEMM, pinned H2D x, D2H y, host sync"},
+        "cpu_baseline": None,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_decode(args, rank, world, local):
     import torch
 
@@ -661,7 +819,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode"], default="sweep")
+    ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode", "prefill"],
+                    default="sweep")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="large workload on N>1 GPUs: all-gather fused into the GEMV (peer "
@@ -678,6 +837,8 @@ def main():
             run_reference(args, rank, world)
         elif args.workload == "decode":
             run_decode(args, rank, world, local)
+        elif args.workload == "prefill":
+            run_prefill(args, rank, world, local)
         else:
             run_gemv_workload(args, rank, world, local)
     finally:

@@ -28,17 +28,20 @@ namespace w4 {
 
 namespace {
 
-constexpr int kBM = 128;         // rows of Y per CTA (MMA M)
-constexpr int kBN = 128;         // columns of Y per CTA (MMA N)
-constexpr int kBK = 64;          // k per ring stage (one 128-byte swizzle row of fp16)
-constexpr int kStages = 4;       // TMA ring
-constexpr int kBStages = 2;      // dequantised W buffers
-constexpr int kGemmThreads = 192;  // warp 0 TMA, warps 1-4 dequant + epilogue, warp 5 MMA
-constexpr int kXBytes = kBM * kBK * 2;             // 16 KB
+constexpr int kUM = 128;          // MMA M (rows of one accumulator)
+constexpr int kBM = 2 * kUM;      // rows of Y per CTA: two accumulators share each W tile
+constexpr int kBN = 128;          // columns of Y per CTA (MMA N)
+constexpr int kBK = 64;           // k per ring stage (one 128-byte swizzle row of fp16)
+constexpr int kStages = 3;        // TMA ring
+constexpr int kBStages = 3;       // dequantised W buffers
+constexpr int kDqWarps = 8;       // dequant (and epilogue) warps
+constexpr int kMmaWarp = 1 + kDqWarps;
+constexpr int kGemmThreads = 32 * (kMmaWarp + 1);  // warp 0 TMA, 1..8 dequant, 9 MMA
+constexpr int kXBytes = kBM * kBK * 2;             // 32 KB
 constexpr int kBBytes = kBN * kBK * 2;             // 16 KB
 constexpr int kPkBytes = (kBK / 8) * kBN * 4;      // 4 KB of packed words
 constexpr int kScBytes = kBN * 2;                  // 256 B of scales
-constexpr int kTmemCols = 128;                     // fp32 accumulator columns
+constexpr int kTmemCols = 2 * kBN;                 // two fp32 accumulators
 constexpr int kErrGemmWait = 7;
 
 struct GemmParams {
@@ -199,17 +202,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&full_tma[i], 1);
-      mbar_init(&empty_tma[i], 4 + 1);  // four dequant warps + the MMA commit
+      mbar_init(&empty_tma[i], kDqWarps + 1);  // the dequant warps + the MMA commit
     }
     for (int i = 0; i < kBStages; ++i) {
-      mbar_init(&full_b[i], 4);
+      mbar_init(&full_b[i], kDqWarps);
       mbar_init(&empty_b[i], 1);
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {  // tensor memory for the 128 x 128 fp32 accumulator
+  if (warp == kMmaWarp) {  // tensor memory for the two 128 x 128 fp32 accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols)
@@ -249,10 +252,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int j = issued - kStages > 0 ? issued - kStages : 0; j < issued; ++j)
         if (!mbar_wait(&full_tma[j % kStages], (j / kStages) & 1)) give_up(kErrDrainWait);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
-      constexpr uint32_t idesc = f16_idesc(kBF16 ? 1 : 0, kBM, kBN);
+      constexpr uint32_t idesc = f16_idesc(kBF16 ? 1 : 0, kUM, kBN);
       int done = 0;
       for (int kt = 0; kt < KT && !stopped(); ++kt) {
         const int s = kt % kStages, sb = kt % kBStages;
@@ -265,9 +268,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t xa = smem_u32(base + kOffX + s * kXBytes);
         const uint32_t ba = smem_u32(base + kOffB + sb * kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)  // 16 k = 32 bytes along the swizzled row
-          umma_f16(tmem_d, kmajor_sw128_desc(xa + kk * 32), kmajor_sw128_desc(ba + kk * 32), idesc,
-                   (kt > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 k = 32 bytes along the swizzled row
+          const uint64_t bd = kmajor_sw128_desc(ba + kk * 32);
+          const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+          // rows 0..127 -> columns 0..127; rows 128..255 (16 KB further) -> 128..255
+          umma_f16(tmem_d, kmajor_sw128_desc(xa + kk * 32), bd, idesc, acc);
+          umma_f16(tmem_d + kBN, kmajor_sw128_desc(xa + kUM * 128 + kk * 32), bd, idesc, acc);
+        }
         umma_commit(&empty_tma[s]);
         umma_commit(&empty_b[sb]);
         ++done;
@@ -277,7 +284,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ dequant
-    const int n = threadIdx.x - 32;  // column of the tile, 0..127
+    const int dt = threadIdx.x - 32;
+    const int n = dt % kBN;           // column of the tile
+    const int jh = (dt / kBN) * 4;    // this thread's 4 of the column's 8 words
     for (int kt = 0; kt < KT && !stopped(); ++kt) {
       const int s = kt % kStages, sb = kt % kBStages;
       if (!mbar_wait(&full_tma[s], (kt / kStages) & 1) ||
@@ -290,12 +299,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t s2 = (uint32_t)sbits | ((uint32_t)sbits << 16);
       const float sf = __half2float(__ushort_as_half(sbits));
       uint8_t* brow = base + kOffB + sb * kBBytes + n * 128;  // row n: 64 k of column n
-      uint32_t wv[8];
+      uint32_t wv[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) wv[j] = pk[j * kBN + n];
+      for (int j = 0; j < 4; ++j) wv[j] = pk[(jh + j) * kBN + n];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)  // chunk j (k 8j..8j+7) lands at chunk j ^ (row % 8)
-        *reinterpret_cast<uint4*>(brow + ((j ^ (n & 7)) << 4)) =
+      for (int j = 0; j < 4; ++j)  // chunk j (k 8j..8j+7) lands at chunk j ^ (row % 8)
+        *reinterpret_cast<uint4*>(brow + (((jh + j) ^ (n & 7)) << 4)) =
             dequant_word<kBF16>(wv[j], s2, sf);
       fence_async_shared();
       __syncwarp();
@@ -308,12 +317,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (!mbar_wait(acc_full, 0)) give_up(kErrGemmWait);
     tc_fence_after();
     if (!stopped()) {
-      const int q = warp & 3;  // this warp's 32-lane slice of tensor memory
-      const int row = m0 + 32 * q + lane;
+      const int q = warp & 3;            // this warp's 32-lane slice of tensor memory
+      const int half = (warp - 1) / 4;   // which accumulator (rows 0..127 or 128..255)
+      const int row = m0 + half * kUM + 32 * q + lane;
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem_d + ((uint32_t)(32 * q) << 16) + 32 * c, r);
+        tmem_ld32(tmem_d + ((uint32_t)(32 * q) << 16) + half * kBN + 32 * c, r);
         if (row < p.M) {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) +
                                                 (size_t)row * p.N + n0 + 32 * c);
@@ -341,7 +351,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     // every MMA has completed (acc_full) before its tensor memory is freed
     if (lane == 0 && !mbar_wait(acc_full, 0)) give_up(kErrGemmWait);
     __syncwarp();
