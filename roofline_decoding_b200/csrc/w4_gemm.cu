@@ -30,18 +30,13 @@ namespace {
 
 constexpr int kUM = 128;          // MMA M (rows of one accumulator)
 constexpr int kBM = 2 * kUM;      // rows of Y per CTA: two accumulators share each W tile
-constexpr int kBN = 128;          // columns of Y per CTA (MMA N)
 constexpr int kBK = 64;           // k per ring stage (one 128-byte swizzle row of fp16)
 constexpr int kStages = 3;        // TMA ring
 constexpr int kBStages = 3;       // dequantised W buffers
 constexpr int kDqWarps = 8;       // dequant (and epilogue) warps
 constexpr int kMmaWarp = 1 + kDqWarps;
 constexpr int kGemmThreads = 32 * (kMmaWarp + 1);  // warp 0 TMA, 1..8 dequant, 9 MMA
-constexpr int kXBytes = kBM * kBK * 2;             // 32 KB
-constexpr int kBBytes = kBN * kBK * 2;             // 16 KB
-constexpr int kPkBytes = (kBK / 8) * kBN * 4;      // 4 KB of packed words
-constexpr int kScBytes = kBN * 2;                  // 256 B of scales
-constexpr int kTmemCols = 2 * kBN;                 // two fp32 accumulators
+constexpr int kNumBars = 2 * kStages + 2 * kBStages + 1;
 constexpr int kErrGemmWait = 7;
 
 struct GemmParams {
@@ -51,21 +46,32 @@ struct GemmParams {
   int* err;
 };
 
-// Shared memory layout (base 1024-aligned): X ring, B buffers, packed ring,
-// scale ring, then the barriers and the tensor-memory address.
-constexpr int kOffX = 0;
-constexpr int kOffB = kOffX + kStages * kXBytes;
-constexpr int kOffPk = kOffB + kBStages * kBBytes;
-constexpr int kOffSc = kOffPk + kStages * kPkBytes;
-constexpr int kOffBar = kOffSc + kStages * kScBytes;
-constexpr int kNumBars = 2 * kStages + 2 * kBStages + 1;
-constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr int kGemmSmem = 1024 + kOffTmem + 16;
-static_assert(kOffB % 1024 == 0 && kXBytes % 1024 == 0 && kBBytes % 1024 == 0,
-              "swizzled operand tiles start on 1024-byte boundaries");
-static_assert(kOffPk % 128 == 0 && kOffSc % 128 == 0 && kPkBytes % 128 == 0 &&
-                  kScBytes % 128 == 0,
-              "tensor-copy destinations are 128-byte aligned");
+// Tile of BN columns (MMA N = BN, 128 or 256) and its shared memory layout
+// (base 1024-aligned): X ring, B buffers, packed ring, scale ring, then the
+// barriers and the tensor-memory address.
+template <int BN>
+struct GemmShape {
+  static constexpr int kXBytes = kBM * kBK * 2;          // 32 KB
+  static constexpr int kBBytes = BN * kBK * 2;           // 16 or 32 KB
+  static constexpr int kPkBytes = (kBK / 8) * BN * 4;    // packed words of a stage
+  static constexpr int kScBytes = BN * 2;                // scales of a stage
+  static constexpr int kTmemCols = 2 * BN;               // two fp32 accumulators
+  static constexpr int kOffX = 0;
+  static constexpr int kOffB = kOffX + kStages * kXBytes;
+  static constexpr int kOffPk = kOffB + kBStages * kBBytes;
+  static constexpr int kOffSc = kOffPk + kStages * kPkBytes;
+  static constexpr int kOffBar = kOffSc + kStages * kScBytes;
+  static constexpr int kOffTmem = kOffBar + kNumBars * 8;
+  static constexpr int kSmem = 1024 + kOffTmem + 16;
+  static constexpr int kThreadsPerCol = kDqWarps * 32 / BN;  // dequant threads per column
+  static constexpr int kWordsPerThread = (kBK / 8) / kThreadsPerCol;
+  static_assert(kOffB % 1024 == 0 && kXBytes % 1024 == 0 && kBBytes % 1024 == 0,
+                "swizzled operand tiles start on 1024-byte boundaries");
+  static_assert(kOffPk % 128 == 0 && kOffSc % 128 == 0 && kPkBytes % 128 == 0 &&
+                    kScBytes % 128 == 0,
+                "tensor-copy destinations are 128-byte aligned");
+  static_assert(kTmemCols <= 512 && kWordsPerThread * kThreadsPerCol == kBK / 8, "tile");
+};
 
 // ---------------------------------------------------------------- tcgen05
 
@@ -179,24 +185,25 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2, float sf)
   return out;
 }
 
-template <bool kBF16>
+template <bool kBF16, int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const GemmParams p) {
+  using S = GemmShape<BN>;
   extern __shared__ uint8_t smem_gemm[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_gemm) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + S::kOffBar);
   uint64_t* full_tma = bars;                       // X + packed + scales landed
   uint64_t* empty_tma = full_tma + kStages;        // dequant read the words, MMA read X
   uint64_t* full_b = empty_tma + kStages;          // B buffer written
   uint64_t* empty_b = full_b + kBStages;           // MMA read the B buffer
   uint64_t* acc_full = empty_b + kBStages;         // accumulator final
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffTmem);
-  int* abort_flag = reinterpret_cast<int*>(base + kOffTmem + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::kOffTmem);
+  int* abort_flag = reinterpret_cast<int*>(base + S::kOffTmem + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
   const int KT = p.K / kBK;
 
   if (threadIdx.x == 0) {
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == kMmaWarp) {  // tensor memory for the two 128 x 128 fp32 accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
+                 "r"(S::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     tc_fence_before();
@@ -243,10 +250,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         if (stopped()) break;
-        mbar_arrive_expect_tx(&full_tma[s], kXBytes + kPkBytes + kScBytes);
-        tma_load_2d(base + kOffX + s * kXBytes, &tm_x, &full_tma[s], kt * kBK, m0);
-        tma_load_2d(base + kOffPk + s * kPkBytes, &tm_w, &full_tma[s], n0, kt * (kBK / 8));
-        tma_load_2d(base + kOffSc + s * kScBytes, &tm_s, &full_tma[s], n0, (kt * kBK) / 128);
+        mbar_arrive_expect_tx(&full_tma[s], S::kXBytes + S::kPkBytes + S::kScBytes);
+        tma_load_2d(base + S::kOffX + s * S::kXBytes, &tm_x, &full_tma[s], kt * kBK, m0);
+        tma_load_2d(base + S::kOffPk + s * S::kPkBytes, &tm_w, &full_tma[s], n0, kt * (kBK / 8));
+        tma_load_2d(base + S::kOffSc + s * S::kScBytes, &tm_s, &full_tma[s], n0, (kt * kBK) / 128);
         ++issued;
       }
       for (int j = issued - kStages > 0 ? issued - kStages : 0; j < issued; ++j)
@@ -255,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
-      constexpr uint32_t idesc = f16_idesc(kBF16 ? 1 : 0, kUM, kBN);
+      constexpr uint32_t idesc = f16_idesc(kBF16 ? 1 : 0, kUM, BN);
       int done = 0;
       for (int kt = 0; kt < KT && !stopped(); ++kt) {
         const int s = kt % kStages, sb = kt % kBStages;
@@ -265,15 +272,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t xa = smem_u32(base + kOffX + s * kXBytes);
-        const uint32_t ba = smem_u32(base + kOffB + sb * kBBytes);
+        const uint32_t xa = smem_u32(base + S::kOffX + s * S::kXBytes);
+        const uint32_t ba = smem_u32(base + S::kOffB + sb * S::kBBytes);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 k = 32 bytes along the swizzled row
           const uint64_t bd = kmajor_sw128_desc(ba + kk * 32);
           const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
           // rows 0..127 -> columns 0..127; rows 128..255 (16 KB further) -> 128..255
           umma_f16(tmem_d, kmajor_sw128_desc(xa + kk * 32), bd, idesc, acc);
-          umma_f16(tmem_d + kBN, kmajor_sw128_desc(xa + kUM * 128 + kk * 32), bd, idesc, acc);
+          umma_f16(tmem_d + BN, kmajor_sw128_desc(xa + kUM * 128 + kk * 32), bd, idesc, acc);
         }
         umma_commit(&empty_tma[s]);
         umma_commit(&empty_b[sb]);
@@ -285,8 +292,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ dequant
     const int dt = threadIdx.x - 32;
-    const int n = dt % kBN;           // column of the tile
-    const int jh = (dt / kBN) * 4;    // this thread's 4 of the column's 8 words
+    const int n = dt % BN;                                  // column of the tile
+    const int jh = (dt / BN) * S::kWordsPerThread;          // this thread's words of the column
     for (int kt = 0; kt < KT && !stopped(); ++kt) {
       const int s = kt % kStages, sb = kt % kBStages;
       if (!mbar_wait(&full_tma[s], (kt / kStages) & 1) ||
@@ -294,16 +301,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         give_up(kErrGemmWait);
         break;
       }
-      const uint32_t* pk = reinterpret_cast<const uint32_t*>(base + kOffPk + s * kPkBytes);
-      const uint16_t sbits = reinterpret_cast<const uint16_t*>(base + kOffSc + s * kScBytes)[n];
+      const uint32_t* pk = reinterpret_cast<const uint32_t*>(base + S::kOffPk + s * S::kPkBytes);
+      const uint16_t sbits = reinterpret_cast<const uint16_t*>(base + S::kOffSc + s * S::kScBytes)[n];
       const uint32_t s2 = (uint32_t)sbits | ((uint32_t)sbits << 16);
       const float sf = __half2float(__ushort_as_half(sbits));
-      uint8_t* brow = base + kOffB + sb * kBBytes + n * 128;  // row n: 64 k of column n
-      uint32_t wv[4];
+      uint8_t* brow = base + S::kOffB + sb * S::kBBytes + n * 128;  // row n: 64 k of column n
+      uint32_t wv[S::kWordsPerThread];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) wv[j] = pk[(jh + j) * kBN + n];
+      for (int j = 0; j < S::kWordsPerThread; ++j) wv[j] = pk[(jh + j) * BN + n];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)  // chunk j (k 8j..8j+7) lands at chunk j ^ (row % 8)
+      for (int j = 0; j < S::kWordsPerThread; ++j)  // chunk j lands at chunk j ^ (row % 8)
         *reinterpret_cast<uint4*>(brow + (((jh + j) ^ (n & 7)) << 4)) =
             dequant_word<kBF16>(wv[j], s2, sf);
       fence_async_shared();
@@ -321,10 +328,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int half = (warp - 1) / 4;   // which accumulator (rows 0..127 or 128..255)
       const int row = m0 + half * kUM + 32 * q + lane;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem_d + ((uint32_t)(32 * q) << 16) + half * kBN + 32 * c, r);
-        if (row < p.M) {
+        tmem_ld32(tmem_d + ((uint32_t)(32 * q) << 16) + half * BN + 32 * c, r);
+        if (row < p.M && n0 + 32 * c < p.N) {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.y) +
                                                 (size_t)row * p.N + n0 + 32 * c);
 #pragma unroll
@@ -357,7 +364,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d),
-                 "r"(kTmemCols)
+                 "r"(S::kTmemCols)
                  : "memory");
   }
 }
@@ -379,18 +386,30 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem, const void* g
 }  // namespace
 
 int gemm_init_device(const DeviceInfo& di) {
-  void* ks[2] = {reinterpret_cast<void*>(&w4_gemm_kernel<false>),
-                 reinterpret_cast<void*>(&w4_gemm_kernel<true>)};
-  if ((size_t)kGemmSmem > (size_t)di.max_smem_optin)
-    return fail(W4_ERR_UNSUPPORTED, "w4_gemm needs %d B of shared memory", kGemmSmem);
-  for (void* k : ks) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  struct K {
+    void* fn;
+    int smem;
+  } ks[4] = {{reinterpret_cast<void*>(&w4_gemm_kernel<false, 128>), GemmShape<128>::kSmem},
+             {reinterpret_cast<void*>(&w4_gemm_kernel<true, 128>), GemmShape<128>::kSmem},
+             {reinterpret_cast<void*>(&w4_gemm_kernel<false, 256>), GemmShape<256>::kSmem},
+             {reinterpret_cast<void*>(&w4_gemm_kernel<true, 256>), GemmShape<256>::kSmem}};
+  for (const K& k : ks) {
+    if ((size_t)k.smem > (size_t)di.max_smem_optin)
+      return fail(W4_ERR_UNSUPPORTED, "w4_gemm needs %d B of shared memory", k.smem);
+    cudaError_t e = cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4_gemm smem)");
-    e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+    e = cudaFuncSetAttribute(k.fn, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(w4_gemm carveout)");
   }
   return W4_OK;
+}
+
+// Tile width: 256 columns halve the re-reads of X per FLOP; 128 when a
+// 256-wide grid would not cover the SMs.
+static int gemm_tile_n(int M, int N, int sms) {
+  const long long tiles256 = (long long)((N + 255) / 256) * ((M + kBM - 1) / kBM);
+  return (N % 256 == 0 || N > 1024) && tiles256 >= sms ? 256 : 128;
 }
 
 int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
@@ -399,13 +418,14 @@ int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* sc
   int st = current_device(&dev);
   if (st != W4_OK) return st;
   const DeviceInfo& di = device_info(dev);
+  const int BN = gemm_tile_n(M, N, di.sm_count > 0 ? di.sm_count : 148);
   CUtensorMap tm_x, tm_w, tm_s;
   if (!encode_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
                  2, x, (uint64_t)K, (uint64_t)M, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, packed, (uint64_t)N, (uint64_t)(K / 8),
-                 kBN, kBK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+                 (uint32_t)BN, kBK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !encode_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, (uint64_t)N,
-                 (uint64_t)(K / 128), kBN, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+                 (uint64_t)(K / 128), (uint32_t)BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
     return fail(W4_ERR_CUDA, "cuTensorMapEncodeTiled failed for w4_gemm M=%d K=%d N=%d", M, K, N);
   GemmParams p;
   p.y = y;
@@ -416,12 +436,17 @@ int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* sc
   p.y_bf16 = y_bf16;
   p.err = di.err_word;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(N / kBN), (unsigned)((M + kBM - 1) / kBM), 1);
+  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + kBM - 1) / kBM), 1);
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = kGemmSmem;
+  cfg.dynamicSmemBytes = BN == 256 ? GemmShape<256>::kSmem : GemmShape<128>::kSmem;
   cfg.stream = stream;
-  cudaError_t e = x_bf16 ? cudaLaunchKernelEx(&cfg, w4_gemm_kernel<true>, tm_x, tm_w, tm_s, p)
-                         : cudaLaunchKernelEx(&cfg, w4_gemm_kernel<false>, tm_x, tm_w, tm_s, p);
+  cudaError_t e;
+  if (BN == 256)
+    e = x_bf16 ? cudaLaunchKernelEx(&cfg, w4_gemm_kernel<true, 256>, tm_x, tm_w, tm_s, p)
+               : cudaLaunchKernelEx(&cfg, w4_gemm_kernel<false, 256>, tm_x, tm_w, tm_s, p);
+  else
+    e = x_bf16 ? cudaLaunchKernelEx(&cfg, w4_gemm_kernel<true, 128>, tm_x, tm_w, tm_s, p)
+               : cudaLaunchKernelEx(&cfg, w4_gemm_kernel<false, 128>, tm_x, tm_w, tm_s, p);
   return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_gemm launch");
 }
 
