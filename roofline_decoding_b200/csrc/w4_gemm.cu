@@ -29,7 +29,7 @@ namespace w4 {
 namespace {
 
 constexpr int kUM = 128;          // MMA M (rows of one accumulator)
-constexpr int kBM = 2 * kUM;      // rows of Y per CTA: two accumulators share each W tile
+constexpr int kBMMax = 2 * kUM;   // rows of Y per CTA: up to two accumulators share a W tile
 constexpr int kBK = 64;           // k per ring stage (one 128-byte swizzle row of fp16)
 constexpr int kStages = 3;        // TMA ring
 constexpr int kBStages = 3;       // dequantised W buffers
@@ -49,13 +49,14 @@ struct GemmParams {
 // Tile of BN columns (MMA N = BN, 128 or 256) and its shared memory layout
 // (base 1024-aligned): X ring, B buffers, packed ring, scale ring, then the
 // barriers and the tensor-memory address.
-template <int BN>
+template <int BN, int NACC>
 struct GemmShape {
-  static constexpr int kXBytes = kBM * kBK * 2;          // 32 KB
+  static constexpr int kBM = NACC * kUM;                 // rows of Y per CTA
+  static constexpr int kXBytes = kBM * kBK * 2;          // 16 or 32 KB
   static constexpr int kBBytes = BN * kBK * 2;           // 16 or 32 KB
   static constexpr int kPkBytes = (kBK / 8) * BN * 4;    // packed words of a stage
   static constexpr int kScBytes = BN * 2;                // scales of a stage
-  static constexpr int kTmemCols = 2 * BN;               // two fp32 accumulators
+  static constexpr int kTmemCols = NACC * BN;            // fp32 accumulators
   static constexpr int kOffX = 0;
   static constexpr int kOffB = kOffX + kStages * kXBytes;
   static constexpr int kOffPk = kOffB + kBStages * kBBytes;
@@ -185,11 +186,11 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t s2, float sf)
   return out;
 }
 
-template <bool kBF16, int BN>
+template <bool kBF16, int BN, int NACC>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w4_gemm_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const GemmParams p) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, NACC>;
   extern __shared__ uint8_t smem_gemm[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_gemm) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int* abort_flag = reinterpret_cast<int*>(base + S::kOffTmem + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * S::kBM;
   const int KT = p.K / kBK;
 
   if (threadIdx.x == 0) {
@@ -278,9 +279,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 k = 32 bytes along the swizzled row
           const uint64_t bd = kmajor_sw128_desc(ba + kk * 32);
           const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
-          // rows 0..127 -> columns 0..127; rows 128..255 (16 KB further) -> 128..255
-          umma_f16(tmem_d, kmajor_sw128_desc(xa + kk * 32), bd, idesc, acc);
-          umma_f16(tmem_d + BN, kmajor_sw128_desc(xa + kUM * 128 + kk * 32), bd, idesc, acc);
+          // accumulator a: rows 128a.. (16 KB further per 128 rows), columns a*BN..
+#pragma unroll
+          for (int a = 0; a < NACC; ++a)
+            umma_f16(tmem_d + a * BN, kmajor_sw128_desc(xa + a * kUM * 128 + kk * 32), bd, idesc,
+                     acc);
         }
         umma_commit(&empty_tma[s]);
         umma_commit(&empty_b[sb]);
@@ -326,6 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (!stopped()) {
       const int q = warp & 3;            // this warp's 32-lane slice of tensor memory
       const int half = (warp - 1) / 4;   // which accumulator (rows 0..127 or 128..255)
+      if (half >= NACC) goto epilogue_done;
       const int row = m0 + half * kUM + 32 * q + lane;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -355,6 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+  epilogue_done:
     tc_fence_before();
   }
   __syncthreads();
@@ -385,14 +390,21 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem, const void* g
 
 }  // namespace
 
+template <bool B, int BN, int NACC>
+void* gemm_fn() {
+  return reinterpret_cast<void*>(&w4_gemm_kernel<B, BN, NACC>);
+}
+
 int gemm_init_device(const DeviceInfo& di) {
   struct K {
     void* fn;
     int smem;
-  } ks[4] = {{reinterpret_cast<void*>(&w4_gemm_kernel<false, 128>), GemmShape<128>::kSmem},
-             {reinterpret_cast<void*>(&w4_gemm_kernel<true, 128>), GemmShape<128>::kSmem},
-             {reinterpret_cast<void*>(&w4_gemm_kernel<false, 256>), GemmShape<256>::kSmem},
-             {reinterpret_cast<void*>(&w4_gemm_kernel<true, 256>), GemmShape<256>::kSmem}};
+  } ks[6] = {{gemm_fn<false, 128, 1>(), GemmShape<128, 1>::kSmem},
+             {gemm_fn<true, 128, 1>(), GemmShape<128, 1>::kSmem},
+             {gemm_fn<false, 128, 2>(), GemmShape<128, 2>::kSmem},
+             {gemm_fn<true, 128, 2>(), GemmShape<128, 2>::kSmem},
+             {gemm_fn<false, 256, 2>(), GemmShape<256, 2>::kSmem},
+             {gemm_fn<true, 256, 2>(), GemmShape<256, 2>::kSmem}};
   for (const K& k : ks) {
     if ((size_t)k.smem > (size_t)di.max_smem_optin)
       return fail(W4_ERR_UNSUPPORTED, "w4_gemm needs %d B of shared memory", k.smem);
@@ -407,9 +419,14 @@ int gemm_init_device(const DeviceInfo& di) {
 
 // Tile width: 256 columns halve the re-reads of X per FLOP; 128 when a
 // 256-wide grid would not cover the SMs.
-static int gemm_tile_n(int M, int N, int sms) {
-  const long long tiles256 = (long long)((N + 255) / 256) * ((M + kBM - 1) / kBM);
-  return (N % 256 == 0 || N > 1024) && tiles256 >= sms ? 256 : 128;
+// Two accumulators (256 rows) share every dequantised W tile, which halves
+// the dequantisation per FLOP; one only when M fits 128 rows.
+static int gemm_tile(int M, int N, int sms, int* nacc) {
+  const long long m2 = (M + kBMMax - 1) / kBMMax;
+  *nacc = M <= kUM ? 1 : 2;
+  if (*nacc == 2 && (N % 256 == 0 || N > 1024) && (long long)((N + 255) / 256) * m2 >= sms)
+    return 256;
+  return 128;
 }
 
 int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
@@ -418,10 +435,12 @@ int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* sc
   int st = current_device(&dev);
   if (st != W4_OK) return st;
   const DeviceInfo& di = device_info(dev);
-  const int BN = gemm_tile_n(M, N, di.sm_count > 0 ? di.sm_count : 148);
+  int nacc = 2;
+  const int BN = gemm_tile(M, N, di.sm_count > 0 ? di.sm_count : 148, &nacc);
+  const int BM = nacc * kUM;
   CUtensorMap tm_x, tm_w, tm_s;
   if (!encode_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                 2, x, (uint64_t)K, (uint64_t)M, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                 2, x, (uint64_t)K, (uint64_t)M, kBK, (uint32_t)BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, packed, (uint64_t)N, (uint64_t)(K / 8),
                  (uint32_t)BN, kBK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
       !encode_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, (uint64_t)N,
@@ -436,17 +455,22 @@ int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* sc
   p.y_bf16 = y_bf16;
   p.err = di.err_word;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + kBM - 1) / kBM), 1);
+  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), 1);
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = BN == 256 ? GemmShape<256>::kSmem : GemmShape<128>::kSmem;
   cfg.stream = stream;
-  cudaError_t e;
-  if (BN == 256)
-    e = x_bf16 ? cudaLaunchKernelEx(&cfg, w4_gemm_kernel<true, 256>, tm_x, tm_w, tm_s, p)
-               : cudaLaunchKernelEx(&cfg, w4_gemm_kernel<false, 256>, tm_x, tm_w, tm_s, p);
-  else
-    e = x_bf16 ? cudaLaunchKernelEx(&cfg, w4_gemm_kernel<true, 128>, tm_x, tm_w, tm_s, p)
-               : cudaLaunchKernelEx(&cfg, w4_gemm_kernel<false, 128>, tm_x, tm_w, tm_s, p);
+  void* fn;
+  if (BN == 256) {
+    cfg.dynamicSmemBytes = GemmShape<256, 2>::kSmem;
+    fn = x_bf16 ? gemm_fn<true, 256, 2>() : gemm_fn<false, 256, 2>();
+  } else if (nacc == 2) {
+    cfg.dynamicSmemBytes = GemmShape<128, 2>::kSmem;
+    fn = x_bf16 ? gemm_fn<true, 128, 2>() : gemm_fn<false, 128, 2>();
+  } else {
+    cfg.dynamicSmemBytes = GemmShape<128, 1>::kSmem;
+    fn = x_bf16 ? gemm_fn<true, 128, 1>() : gemm_fn<false, 128, 1>();
+  }
+  void* args[] = {&tm_x, &tm_w, &tm_s, &p};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
   return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_gemm launch");
 }
 

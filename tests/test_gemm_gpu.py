@@ -38,7 +38,9 @@ def _want(x, packed, scales, bf16_weights=False):
                                    (1024, 1536, 1536), (1, 512, 128), (200, 4096, 1024),
                                    # grids of >= 148 256-wide tiles: the 256-column tile,
                                    # the second with a half-filled last tile (N % 256 = 128)
-                                   (2048, 512, 4864), (4000, 256, 2432)])
+                                   (2048, 512, 4864), (4000, 256, 2432),
+                                   # 128-column tiles of 256 rows (two accumulators)
+                                   (5700, 128, 896), (600, 384, 640)])
 def test_gemm_fp16_matches_oracle(M, K, N):
     x, packed, scales = _case(M, K, N, seed=M + K)
     y = Kn.w4_gemm(x.cuda(), packed, scales).float().cpu()
