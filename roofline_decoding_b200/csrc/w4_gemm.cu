@@ -24,6 +24,8 @@
 #include "w4_internal.h"
 #include "w4_ptx.cuh"
 
+#include <algorithm>
+
 namespace w4 {
 
 namespace {
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * S::kBM;
   const int KT = p.K / kBK;
+  constexpr int kt0 = 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -252,9 +255,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (stopped()) break;
         mbar_arrive_expect_tx(&full_tma[s], S::kXBytes + S::kPkBytes + S::kScBytes);
-        tma_load_2d(base + S::kOffX + s * S::kXBytes, &tm_x, &full_tma[s], kt * kBK, m0);
-        tma_load_2d(base + S::kOffPk + s * S::kPkBytes, &tm_w, &full_tma[s], n0, kt * (kBK / 8));
-        tma_load_2d(base + S::kOffSc + s * S::kScBytes, &tm_s, &full_tma[s], n0, (kt * kBK) / 128);
+        const int kg = kt0 + kt;  // stage of the whole K
+        tma_load_2d(base + S::kOffX + s * S::kXBytes, &tm_x, &full_tma[s], kg * kBK, m0);
+        tma_load_2d(base + S::kOffPk + s * S::kPkBytes, &tm_w, &full_tma[s], n0, kg * (kBK / 8));
+        tma_load_2d(base + S::kOffSc + s * S::kScBytes, &tm_s, &full_tma[s], n0, (kg * kBK) / 128);
         ++issued;
       }
       for (int j = issued - kStages > 0 ? issued - kStages : 0; j < issued; ++j)
