@@ -11,8 +11,10 @@
  * outputs y are [M, N] row-major fp16 or bf16.
  *
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
- * passed as void*. None of them allocates, frees or synchronises, so they
- * can be recorded into a CUDA graph once w4_init() has run on the device.
+ * passed as void*. None of the compute entry points allocates, frees or
+ * synchronises, so they can be recorded into a CUDA graph once w4_init()
+ * has run on the device. The w4_peer_* memory calls near the end are the
+ * exception: they allocate, map and free, and belong outside any capture.
  * All return a w4_status; a non-zero status means nothing was launched.
  */
 #ifndef W4B200_H_
@@ -157,7 +159,8 @@ int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scale
  * Buffers come from w4_peer_alloc on each rank and are opened on the others
  * with w4_peer_open (CUDA IPC). The output alternates between two buffers by
  * epoch parity, so a rank that runs ahead never overwrites a y that a slower
- * rank may still read; call k writes y[k % 2]. */
+ * rank may still read; the k-th call on a group (counting from 1) writes
+ * y[k % 2]. */
 #define W4B200_MAX_PEERS 8
 typedef struct w4_peer_out {
   int world, rank;             /* ranks in the group, this rank */
@@ -175,9 +178,10 @@ size_t w4_peer_flag_bytes(int world);
 /* y = x @ dequant(W_local) on this rank's columns, gathered into every
  * rank's y[epoch % 2] (see above). N is the local column count; y_dtype the
  * type of y. Blocks (bounded, 1 s) until every rank of the group ran the same
- * call; a rank that never arrives sets the device error word. Returns the
- * parity written through *parity (read after the stream completes: the
- * epoch lives on the device, so the host passes the parity it expects). */
+ * call; a rank that never arrives sets the device error word. The epoch
+ * counter lives on the device (state[0]); the host counts its own calls on
+ * the group to know which of y[0] / y[1] the k-th call filled (y[k % 2],
+ * k counted from 1). */
 int w4_gemv_allgather(const void* x, int x_dtype, const int32_t* packed,
                       const void* scales, int y_dtype, int M, int K, int N,
                       const w4_gemv_config* cfg, const w4_peer_out* peers,
