@@ -335,7 +335,6 @@ def run_gemv_workload(args, rank, world, local):
     stream = torch.cuda.Stream(device)
     peers = None
     if sharded and args.gather == "peer":
-        from roofline_decoding_b200._lib import GemvConfig
         from roofline_decoding_b200.sharded import PeerGroup
 
         peers = PeerGroup(device=device)
@@ -347,7 +346,7 @@ def run_gemv_workload(args, rank, world, local):
             for i, (M, K, N, dt) in enumerate(cases):
                 p, s = pool[si][i]
                 c = cfgs[i]
-                c = GemvConfig(c.strips, c.row_groups, c.stages, c.split, 1 if pdl else 0)
+                c = c.with_pdl(1 if pdl else 0)
                 peers.gemv(xs[i], p, s, f"case{i}", N, rank * n_loc[i], config=c)
             return
         for i in range(n_launch):
@@ -493,13 +492,11 @@ def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
     exceed 3x L2, so each launch streams from HBM as in a decode step; the
     chain is long enough that event resolution does not matter.
     """
-    from roofline_decoding_b200._lib import GemvConfig
-
     packed, scales = weights
     wbytes = packed.numel() * 4 + scales.numel() * 2
     n = int(min(2048, max(8, -(-3 * l2 // wbytes))))
     copies = [(packed.clone(), scales.clone()) for _ in range(n)]
-    c = GemvConfig(cfg.strips, cfg.row_groups, cfg.stages, cfg.split, 1)
+    c = cfg.with_pdl(1)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(g, stream=stream):

@@ -27,6 +27,8 @@ class W4Error(RuntimeError):
 
 
 class GemvConfig(ctypes.Structure):
+    """w4_gemv_config (include/w4b200.h), as a tuple (strips, row_groups,
+    stages, split, pdl)."""
     _fields_ = [
         ("strips", ctypes.c_int),
         ("row_groups", ctypes.c_int),
@@ -41,6 +43,12 @@ class GemvConfig(ctypes.Structure):
     @classmethod
     def from_tuple(cls, t) -> "GemvConfig":
         return cls(*[int(v) for v in t])
+
+    def with_pdl(self, pdl: int) -> "GemvConfig":
+        """A copy with programmatic dependent launch switched on (1) or off (0)."""
+        c = GemvConfig.from_tuple(self.as_tuple())
+        c.pdl = int(pdl)
+        return c
 
     def __repr__(self) -> str:
         return ("GemvConfig(strips=%d, row_groups=%d, stages=%d, split=%d, pdl=%d)"

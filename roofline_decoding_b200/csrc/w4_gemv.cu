@@ -169,6 +169,308 @@ __device__ __forceinline__ uint4 permute_row(uint4 v) {
 }
 
 
+// Stages the activations of K groups [g0, g1) of every batch row in shared
+// memory, in the order the MMA fragments consume them (permute_row), with the
+// prologue applied; leaves beta[m][group] (the unpack constant summed against
+// the group's activations) and, for RMSNorm, 1/rms per row. Run by the kCW
+// compute warps only; ends with a barrier among them.
+template <bool kBF16, int kCW>
+__device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, int g1, int gps,
+                                                  uint8_t* s_x, int plane, float* s_beta,
+                                                  float* s_inv, float* s_red, int warp,
+                                                  int lane) {
+  constexpr int nct = kCW * 32;
+  const int M = p.M;
+  const int rows_slice = gps * 16;
+  const uint16_t* xg = static_cast<const uint16_t*>(p.x);
+  // x row pitch: a SwiGLU prologue reads gate|up rows of 2K
+  const size_t x_pitch = (p.pro == W4_PRO_SWIGLU) ? 2 * (size_t)p.K : (size_t)p.K;
+  // RMSNorm needs 1/rms of the whole row. When this CTA stages the whole row
+  // of a single activation row in one batch (the decode case), the sum of
+  // squares comes from the staging loads themselves (one global round
+  // trip); otherwise a pre-pass over the row computes it first.
+  const bool rms_one_pass = p.pro == W4_PRO_RMSNORM && M == 1 && g0 == 0 &&
+                            g1 == p.groups_total && rows_slice <= 4 * nct;
+  if (p.pro == W4_PRO_RMSNORM && !rms_one_pass) {
+    // inv_rms[m] over the whole row (every CTA recomputes it: K <= 28672
+    // activations, served from L2), reduced in a fixed order
+    float* s_part = s_red;  // scratch: [kCW][M] partial sums (s_red is free until the epilogue)
+    for (int m = 0; m < M; ++m) {
+      float acc2 = 0.f;
+      for (int i = threadIdx.x; i < p.K / 8; i += nct) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xg + m * x_pitch + 8 * (size_t)i));
+        const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = h2f2(vi[e], kBF16);
+          acc2 = fmaf(f.x, f.x, acc2);
+          acc2 = fmaf(f.y, f.y, acc2);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+      if (lane == 0) s_part[warp * M + m] = acc2;
+    }
+    consumer_bar_sync(nct);
+    if (threadIdx.x < M) {
+      float tot = 0.f;
+      for (int w = 0; w < kCW; ++w) tot += s_part[w * M + threadIdx.x];
+      s_inv[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
+    }
+    consumer_bar_sync(nct);
+  }
+  // Batches of 4 independent 16-byte loads per thread, all in flight before
+  // the first is consumed (one global round trip per batch, not per row).
+  // 16 consecutive threads hold the 16 rows of one group, so the group's
+  // correction beta is a 16-lane shuffle reduction (nct and rows_slice are
+  // multiples of 16, so a 16-lane group never straddles two groups).
+  const int total = M * rows_slice;
+  // b0 is the same for every consumer thread, so all of them run the same
+  // trips and every shuffle below has its full warp
+  for (int b0 = 0; b0 < total; b0 += 4 * nct) {
+    uint4 v[4], aux[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = b0 + u * nct + threadIdx.x;
+      v[u] = make_uint4(0u, 0u, 0u, 0u);
+      aux[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < total) {
+        const int m = idx / rows_slice;
+        const int krow = g0 * 16 + (idx - m * rows_slice);  // packed row = 8 activations
+        if (krow < g1 * 16) {
+          const uint16_t* xr = xg + (size_t)m * x_pitch + (size_t)krow * 8;
+          v[u] = __ldcg(reinterpret_cast<const uint4*>(xr));
+          if (p.pro == W4_PRO_RMSNORM)
+            aux[u] = __ldg(reinterpret_cast<const uint4*>(
+                static_cast<const uint16_t*>(p.pro_w) + (size_t)krow * 8));
+          else if (p.pro == W4_PRO_SWIGLU)
+            aux[u] = __ldcg(reinterpret_cast<const uint4*>(xr + p.K));
+        }
+      }
+    }
+    if (rms_one_pass) {  // sum of squares of the (whole, single) row from registers
+      float acc2 = 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v[u]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = h2f2(vi[e], kBF16);
+          acc2 = fmaf(f.x, f.x, acc2);
+          acc2 = fmaf(f.y, f.y, acc2);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+      if (lane == 0) s_red[warp] = acc2;
+      consumer_bar_sync(nct);
+      if (threadIdx.x == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kCW; ++w) tot += s_red[w];
+        s_inv[0] = rsqrtf(tot / (float)p.K + p.eps);
+      }
+      consumer_bar_sync(nct);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (b0 + u * nct >= total) break;  // uniform over the consumer threads
+      const int idx = b0 + u * nct + threadIdx.x;
+      float lo = 0.f, hi = 0.f;
+      uint4 o = make_uint4(0u, 0u, 0u, 0u);
+      if (idx < total) {
+        const int m = idx / rows_slice;
+        const int r = idx - m * rows_slice;
+        const int krow = g0 * 16 + r;
+        if (p.pro != W4_PRO_NONE && krow < g1 * 16)
+          v[u] = stage_transform<kBF16>(p.pro, v[u], aux[u],
+                                        p.pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
+        o = permute_row<kBF16>(v[u]);
+        *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
+        const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
+        const float2 c = h2f2(o.z, kBF16), d = h2f2(o.w, kBF16);
+        lo = (a.x + a.y) + (c.x + c.y);
+        hi = (b.x + b.y) + (d.x + d.y);
+      }
+      float bsum = kBF16 ? kBF16Offset * (lo + hi) : kF16LowOffset * lo + kF16HighOffset * hi;
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+      if (idx < total && (idx & 15) == 0) s_beta[idx >> 4] = bsum;
+    }
+  }
+  consumer_bar_sync(nct);
+}
+
+// Shared-memory addresses one compute lane reads in every stage:
+//   weights: rows rg*16 + 8*o + 2t + e of its strip's box, 16-byte chunk g
+//            stored at chunk g ^ (row & 7) by the 128B swizzle;
+//   x:       lanes whose batch row g >= M read row M-1 instead, so every
+//            lane loads unconditionally (their output columns are unused);
+//   beta:    likewise clamped.
+template <int MB, int SW, int RG>
+struct LaneView {
+  uint32_t w_off[2];
+  uint32_t x_off[MB];
+  const float* b_row[MB][2];
+  uint32_t sc_off;
+
+  __device__ __forceinline__ LaneView(const uint8_t* s_w, const uint8_t* s_x, const uint8_t* s_sc,
+                                      const float* s_beta, int plane, int gps, int M, int strip,
+                                      int rg, int g, int t) {
+    using T = TileShape<SW, RG>;
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      w_off[e] = smem_u32(s_w) + strip * T::kStripBytes + (rg * 16 + 2 * t + e) * 128 +
+                 ((g ^ (2 * t + e)) << 4);
+#pragma unroll
+    for (int mb = 0; mb < MB; ++mb) {
+      x_off[mb] = smem_u32(s_x) + min(8 * mb + g, M - 1) * plane + 2 * t * 16;
+      b_row[mb][0] = s_beta + min(8 * mb + 2 * t, M - 1) * gps;
+      b_row[mb][1] = s_beta + min(8 * mb + 2 * t + 1, M - 1) * gps;
+    }
+    sc_off = smem_u32(s_sc) + (rg * T::kNT + 32 * strip + 4 * g) * 2;
+  }
+};
+
+// One K group of one stage for one compute warp: acc += s * sum_k (q - 8) x
+// over the group gl of the staged activations, its weights in the ring slot
+// at byte offset stage_base and its scales in the scale slot at sc.
+template <bool kBF16, int MB, int SW, int RG>
+__device__ __forceinline__ void mma_group(float (&acc)[2][MB][4], const LaneView<MB, SW, RG>& lv,
+                                          uint32_t stage_base, uint32_t sc, int gl) {
+  // accumulators start at -beta of their batch row: the MMA sums then
+  // leave exactly sum_k (q - 8) x of this group
+  float c[2][MB][4];
+#pragma unroll
+  for (int mb = 0; mb < MB; ++mb) {
+    const float nb0 = -lv.b_row[mb][0][gl];
+    const float nb1 = -lv.b_row[mb][1][gl];
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+      c[a][mb][0] = nb0;
+      c[a][mb][1] = nb1;
+      c[a][mb][2] = nb0;
+      c[a][mb][3] = nb1;
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < 2; ++o) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const uint4 wv = lds128(lv.w_off[e] + stage_base + o * 1024);
+      const uint32_t xrow = (gl * 16 + 8 * o + e) * 16;
+      uint4 xb[MB];
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) xb[mb] = lds128(lv.x_off[mb] + xrow);
+      uint32_t ha[4], hb[4];
+      unpack_nibbles<kBF16>(wv.x, ha);  // column 4g
+      unpack_nibbles<kBF16>(wv.y, hb);  // column 4g+1
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) {
+        mma_16816<kBF16>(c[0][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+        mma_16816<kBF16>(c[0][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+      }
+      unpack_nibbles<kBF16>(wv.z, ha);  // column 4g+2
+      unpack_nibbles<kBF16>(wv.w, hb);  // column 4g+3
+#pragma unroll
+      for (int mb = 0; mb < MB; ++mb) {
+        mma_16816<kBF16>(c[1][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+        mma_16816<kBF16>(c[1][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+      }
+    }
+  }
+  // Scales of this group for columns (4g, 4g+1) and (4g+2, 4g+3).
+  const uint32_t s01 = lds32(sc);
+  const uint32_t s23 = lds32(sc + 4);
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&s01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
+#pragma unroll
+  for (int mb = 0; mb < MB; ++mb) {
+    acc[0][mb][0] = fmaf(f01.x, c[0][mb][0], acc[0][mb][0]);
+    acc[0][mb][1] = fmaf(f01.x, c[0][mb][1], acc[0][mb][1]);
+    acc[0][mb][2] = fmaf(f01.y, c[0][mb][2], acc[0][mb][2]);
+    acc[0][mb][3] = fmaf(f01.y, c[0][mb][3], acc[0][mb][3]);
+    acc[1][mb][0] = fmaf(f23.x, c[1][mb][0], acc[1][mb][0]);
+    acc[1][mb][1] = fmaf(f23.x, c[1][mb][1], acc[1][mb][1]);
+    acc[1][mb][2] = fmaf(f23.y, c[1][mb][2], acc[1][mb][2]);
+    acc[1][mb][3] = fmaf(f23.y, c[1][mb][3], acc[1][mb][3]);
+  }
+}
+
+// A compute warp's accumulators into s_red[rg][m][col] (rows m < M only).
+template <int MB, int NT>
+__device__ __forceinline__ void write_partials(const float (&acc)[2][MB][4], float* s_red, int M,
+                                               int strip, int rg, int g, int t) {
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int mb = 0; mb < MB; ++mb)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = 8 * mb + 2 * t + (i & 1);
+        if (m < M) {
+          const int col = 32 * strip + 4 * g + 2 * a + (i >> 1);
+          s_red[(rg * M + m) * NT + col] = acc[a][mb][i];
+        }
+      }
+}
+
+// Writes y[m, n] = v with the epilogue applied (n < N): to y, or for a
+// gathered output to every rank's buffer of this call's parity.
+__device__ __forceinline__ void store_out(const GemvParams& p, const PeerParams& pp,
+                                          unsigned epoch, int m, int n, float v) {
+  if (n >= p.N) return;
+  if (p.epi == W4_EPI_BIAS) {
+    v += ld_f(p.epi_src, n, p.y_bf16);  // one rounding, like a GEMM's bias epilogue
+  } else if (p.epi == W4_EPI_RESIDUAL) {
+    // out = round(residual + round(y)): the layer output is rounded before
+    // the residual add, as in the reference model's bf16 forward
+    v = ld_f(p.epi_src, (size_t)m * p.N + n, p.y_bf16) + round_to(v, p.y_bf16);
+  }
+  if (pp.world > 0) {  // every rank's buffer of this parity (NVLink stores)
+    const size_t at = (size_t)m * pp.n_full + pp.col_off + n;
+    const int par = (int)(epoch & 1u);
+    for (int q = 0; q < pp.world; ++q) {
+      if (p.y_bf16)
+        static_cast<__nv_bfloat16*>(pp.y[par][q])[at] = __float2bfloat16_rn(v);
+      else
+        static_cast<__half*>(pp.y[par][q])[at] = __float2half_rn(v);
+    }
+  } else if (p.y_bf16) {
+    static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v);
+  } else {
+    static_cast<__half*>(p.y)[(size_t)m * p.N + n] = __float2half_rn(v);
+  }
+}
+
+// Gathered output: the CTA that finishes last on this rank publishes the
+// epoch to every rank, then waits until every rank published it here. Each
+// CTA orders its peer stores before its count at GPU scope (a cumulative
+// release); the last CTA, having observed every count, makes all of them
+// visible system-wide with one system-scope fence before it publishes. Call
+// after a __syncthreads that follows the CTA's last store.
+__device__ __forceinline__ void publish_gathered(const GemvParams& p, const PeerParams& pp,
+                                                 unsigned epoch, unsigned ctas) {
+  if (threadIdx.x != 0) return;
+  __threadfence();
+  if (atomicAdd(&pp.state[1], 1u) == ctas - 1) {
+    __threadfence_system();
+    for (int q = 0; q < pp.world; ++q) st_release_sys(pp.flags[q] + pp.rank, epoch);
+    const unsigned* mine = pp.flags[pp.rank];
+    for (int q = 0; q < pp.world; ++q) {
+      const unsigned long long t0 = globaltimer_ns();
+      while ((int)(ld_acquire_sys(mine + q) - epoch) < 0) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          report_error(p.err, kErrPeerWait);
+          break;
+        }
+      }
+    }
+    pp.state[1] = 0u;
+    pp.state[0] = epoch;
+    __threadfence();
+  }
+}
+
 template <bool kBF16, int MB, int SW, int RG>
 __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
     w4_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
@@ -181,15 +483,15 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
 
   const int S = p.stages;
   const int M = p.M;
-  const int rows_slice = p.groups_per_split * 16;
-  const int plane = rows_slice * 16 + 16;  // +16 B: odd batch rows land on other banks
+  const int gps = p.groups_per_split;
+  const int plane = gps * 16 * 16 + 16;  // +16 B: odd batch rows land on other banks
   uint8_t* s_w = smem;
   uint8_t* s_sc = s_w + S * T::kStageBytes;
   uint8_t* s_x = s_sc + S * T::kScaleSlot;
   // beta[m][group]: the constant the unpacked values carry, summed against the
   // staged activations of each group (subtracted through the accumulator init)
   float* s_beta = reinterpret_cast<float*>(s_x + M * plane);
-  float* s_inv = s_beta + ((M * p.groups_per_split + 3) & ~3);  // RMSNorm 1/rms per row
+  float* s_inv = s_beta + ((M * gps + 3) & ~3);  // RMSNorm 1/rms per row
   float* s_red = s_inv + 16;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_red + RG * M * T::kNT);
   uint64_t* empty = full + S;
@@ -198,8 +500,8 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * T::kNT;
-  const int g0 = blockIdx.y * p.groups_per_split;
-  const int g1 = min(p.groups_total, g0 + p.groups_per_split);
+  const int g0 = blockIdx.y * gps;
+  const int g1 = min(p.groups_total, g0 + gps);
   const int n_groups = max(0, g1 - g0);
   const int n_stages = (n_groups + RG - 1) / RG;
 
@@ -221,21 +523,8 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
   // output only after its own grid-dependency wait.
   grid_launch_dependents();
 
-  // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
-  // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
-  float acc[2][MB][4];
-#pragma unroll
-  for (int a = 0; a < 2; ++a)
-#pragma unroll
-    for (int b = 0; b < MB; ++b)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
-
   if (warp == T::kCW) {
     // ------------------------------------------------------------ producer
-    // The launch of a dependent (PDL) grid waits until every thread of every
-    // CTA here has signalled; lanes 1..31 signal at once, lane 0 once all of
-    // this CTA's weight loads are in flight.
     if (lane == 0) {
       int issued = 0;
       int slot = 0;
@@ -265,152 +554,28 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
 
   } else {
     // ------------------------------------------------------------ consumers
-    const int nct = T::kCW * 32;
     // x is produced by the previous kernel on the stream: wait for it.
     grid_dependency_wait();
     // the previous call's last CTA advanced the epoch before that grid ended
     if (pp.world > 0 && threadIdx.x == 0) s_epoch = __ldcg(pp.state) + 1u;
-    const uint16_t* xg = static_cast<const uint16_t*>(p.x);
-    // x row pitch: a SwiGLU prologue reads gate|up rows of 2K
-    const size_t x_pitch = (p.pro == W4_PRO_SWIGLU) ? 2 * (size_t)p.K : (size_t)p.K;
-    // RMSNorm needs 1/rms of the whole row. When this CTA stages the whole row
-    // of a single activation row in one batch (the decode case), the sum of
-    // squares comes from the staging loads themselves (one global round
-    // trip); otherwise a pre-pass over the row computes it first.
-    const bool rms_one_pass = p.pro == W4_PRO_RMSNORM && M == 1 && g0 == 0 &&
-                              g1 == p.groups_total && rows_slice <= 4 * nct;
-    if (p.pro == W4_PRO_RMSNORM && !rms_one_pass) {
-      // inv_rms[m] over the whole row (every CTA recomputes it: K <= 28672
-      // activations, served from L2), reduced in a fixed order
-      float* s_part = s_red;  // scratch: [kCW][M] partial sums (s_red is free until the epilogue)
-      for (int m = 0; m < M; ++m) {
-        float acc2 = 0.f;
-        for (int i = threadIdx.x; i < p.K / 8; i += nct) {
-          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xg + m * x_pitch + 8 * (size_t)i));
-          const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = h2f2(vi[e], kBF16);
-            acc2 = fmaf(f.x, f.x, acc2);
-            acc2 = fmaf(f.y, f.y, acc2);
-          }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
-        if (lane == 0) s_part[warp * M + m] = acc2;
-      }
-      consumer_bar_sync(nct);
-      if (threadIdx.x < M) {
-        float tot = 0.f;
-        for (int w = 0; w < T::kCW; ++w) tot += s_part[w * M + threadIdx.x];
-        s_inv[threadIdx.x] = rsqrtf(tot / (float)p.K + p.eps);
-      }
-      consumer_bar_sync(nct);
-    }
-    // Batches of 4 independent 16-byte loads per thread, all in flight before
-    // the first is consumed (one global round trip per batch, not per row).
-    // 16 consecutive threads hold the 16 rows of one group, so the group's
-    // correction beta is a 16-lane shuffle reduction (nct and rows_slice are
-    // multiples of 16, so a 16-lane group never straddles two groups).
-    const int total = M * rows_slice;
-    // b0 is the same for every consumer thread, so all of them run the same
-    // trips and every shuffle below has its full warp
-    for (int b0 = 0; b0 < total; b0 += 4 * nct) {
-      uint4 v[4], aux[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int idx = b0 + u * nct + threadIdx.x;
-        v[u] = make_uint4(0u, 0u, 0u, 0u);
-        aux[u] = make_uint4(0u, 0u, 0u, 0u);
-        if (idx < total) {
-          const int m = idx / rows_slice;
-          const int krow = g0 * 16 + (idx - m * rows_slice);  // packed row = 8 activations
-          if (krow < g1 * 16) {
-            const uint16_t* xr = xg + (size_t)m * x_pitch + (size_t)krow * 8;
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(xr));
-            if (p.pro == W4_PRO_RMSNORM)
-              aux[u] = __ldg(reinterpret_cast<const uint4*>(
-                  static_cast<const uint16_t*>(p.pro_w) + (size_t)krow * 8));
-            else if (p.pro == W4_PRO_SWIGLU)
-              aux[u] = __ldcg(reinterpret_cast<const uint4*>(xr + p.K));
-          }
-        }
-      }
-      if (rms_one_pass) {  // sum of squares of the (whole, single) row from registers
-        float acc2 = 0.f;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v[u]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = h2f2(vi[e], kBF16);
-            acc2 = fmaf(f.x, f.x, acc2);
-            acc2 = fmaf(f.y, f.y, acc2);
-          }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
-        if (lane == 0) s_red[warp] = acc2;
-        consumer_bar_sync(nct);
-        if (threadIdx.x == 0) {
-          float tot = 0.f;
-          for (int w = 0; w < T::kCW; ++w) tot += s_red[w];
-          s_inv[0] = rsqrtf(tot / (float)p.K + p.eps);
-        }
-        consumer_bar_sync(nct);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (b0 + u * nct >= total) break;  // uniform over the consumer threads
-        const int idx = b0 + u * nct + threadIdx.x;
-        float lo = 0.f, hi = 0.f;
-        uint4 o = make_uint4(0u, 0u, 0u, 0u);
-        if (idx < total) {
-          const int m = idx / rows_slice;
-          const int r = idx - m * rows_slice;
-          const int krow = g0 * 16 + r;
-          if (p.pro != W4_PRO_NONE && krow < g1 * 16)
-            v[u] = stage_transform<kBF16>(p.pro, v[u], aux[u],
-                                          p.pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
-          o = permute_row<kBF16>(v[u]);
-          *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
-          const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
-          const float2 c = h2f2(o.z, kBF16), d = h2f2(o.w, kBF16);
-          lo = (a.x + a.y) + (c.x + c.y);
-          hi = (b.x + b.y) + (d.x + d.y);
-        }
-        float bsum = kBF16 ? kBF16Offset * (lo + hi) : kF16LowOffset * lo + kF16HighOffset * hi;
-#pragma unroll
-        for (int off = 8; off > 0; off >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
-        if (idx < total && (idx & 15) == 0) s_beta[idx >> 4] = bsum;
-      }
-    }
-    consumer_bar_sync(nct);
+    stage_activations<kBF16, T::kCW>(p, g0, g1, gps, s_x, plane, s_beta, s_inv, s_red, warp,
+                                     lane);
 
     const int strip = warp % SW;
     const int rg = warp / SW;
     const int g = lane >> 2;
     const int t = lane & 3;
-    // Per-thread shared-memory offsets, fixed for the whole loop:
-    //   weights: rows rg*16 + 8*o + 2t + e of the strip box, 16-byte chunk g
-    //            stored at chunk g ^ (row & 7) by the 128B swizzle;
-    //   x:       lanes whose batch row g >= M read row M-1 instead, so every
-    //            lane loads unconditionally (their output columns are unused);
-    //   beta:    likewise clamped.
-    uint32_t w_off[2];
+    const LaneView<MB, SW, RG> lv(s_w, s_x, s_sc, s_beta, plane, gps, M, strip, rg, g, t);
+
+    // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
+    // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
+    float acc[2][MB][4];
 #pragma unroll
-    for (int e = 0; e < 2; ++e)
-      w_off[e] = smem_u32(s_w) + strip * T::kStripBytes + (rg * 16 + 2 * t + e) * 128 +
-                 ((g ^ (2 * t + e)) << 4);
-    uint32_t x_off[MB];
-    const float* b_row[MB][2];
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-    for (int mb = 0; mb < MB; ++mb) {
-      x_off[mb] = smem_u32(s_x) + min(8 * mb + g, M - 1) * plane + 2 * t * 16;
-      b_row[mb][0] = s_beta + min(8 * mb + 2 * t, M - 1) * p.groups_per_split;
-      b_row[mb][1] = s_beta + min(8 * mb + 2 * t + 1, M - 1) * p.groups_per_split;
-    }
-    const uint32_t sc_off = smem_u32(s_sc) + (rg * T::kNT + 32 * strip + 4 * g) * 2;
+      for (int b = 0; b < MB; ++b)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
 
     int slot = 0;
     uint32_t phase = 0;
@@ -420,67 +585,9 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
         break;
       }
       const int gl = j * RG + rg;  // group inside the slice
-      if (gl < n_groups) {
-        // accumulators start at -beta of their batch row: the MMA sums then
-        // leave exactly sum_k (q - 8) x of this group
-        float c[2][MB][4];
-#pragma unroll
-        for (int mb = 0; mb < MB; ++mb) {
-          const float nb0 = -b_row[mb][0][gl];
-          const float nb1 = -b_row[mb][1][gl];
-#pragma unroll
-          for (int a = 0; a < 2; ++a) {
-            c[a][mb][0] = nb0;
-            c[a][mb][1] = nb1;
-            c[a][mb][2] = nb0;
-            c[a][mb][3] = nb1;
-          }
-        }
-        const uint32_t stage_base = slot * T::kStageBytes;
-#pragma unroll
-        for (int o = 0; o < 2; ++o) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const uint4 wv = lds128(w_off[e] + stage_base + o * 1024);
-            const uint32_t xrow = (gl * 16 + 8 * o + e) * 16;
-            uint4 xb[MB];
-#pragma unroll
-            for (int mb = 0; mb < MB; ++mb) xb[mb] = lds128(x_off[mb] + xrow);
-            uint32_t ha[4], hb[4];
-            unpack_nibbles<kBF16>(wv.x, ha);  // column 4g
-            unpack_nibbles<kBF16>(wv.y, hb);  // column 4g+1
-#pragma unroll
-            for (int mb = 0; mb < MB; ++mb) {
-              mma_16816<kBF16>(c[0][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
-              mma_16816<kBF16>(c[0][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
-            }
-            unpack_nibbles<kBF16>(wv.z, ha);  // column 4g+2
-            unpack_nibbles<kBF16>(wv.w, hb);  // column 4g+3
-#pragma unroll
-            for (int mb = 0; mb < MB; ++mb) {
-              mma_16816<kBF16>(c[1][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
-              mma_16816<kBF16>(c[1][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
-            }
-          }
-        }
-        // Scales of this group for columns (4g, 4g+1) and (4g+2, 4g+3).
-        const uint32_t sc = sc_off + slot * T::kScaleSlot;
-        const uint32_t s01 = lds32(sc);
-        const uint32_t s23 = lds32(sc + 4);
-        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&s01));
-        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
-#pragma unroll
-        for (int mb = 0; mb < MB; ++mb) {
-          acc[0][mb][0] = fmaf(f01.x, c[0][mb][0], acc[0][mb][0]);
-          acc[0][mb][1] = fmaf(f01.x, c[0][mb][1], acc[0][mb][1]);
-          acc[0][mb][2] = fmaf(f01.y, c[0][mb][2], acc[0][mb][2]);
-          acc[0][mb][3] = fmaf(f01.y, c[0][mb][3], acc[0][mb][3]);
-          acc[1][mb][0] = fmaf(f23.x, c[1][mb][0], acc[1][mb][0]);
-          acc[1][mb][1] = fmaf(f23.x, c[1][mb][1], acc[1][mb][1]);
-          acc[1][mb][2] = fmaf(f23.y, c[1][mb][2], acc[1][mb][2]);
-          acc[1][mb][3] = fmaf(f23.y, c[1][mb][3], acc[1][mb][3]);
-        }
-      }
+      if (gl < n_groups)
+        mma_group<kBF16, MB, SW, RG>(acc, lv, slot * T::kStageBytes,
+                                     lv.sc_off + slot * T::kScaleSlot, gl);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
       if (++slot == S) {
@@ -488,20 +595,7 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
         phase ^= 1u;
       }
     }
-
-    // Per-warp partials into s_red[rg][m][col].
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int mb = 0; mb < MB; ++mb)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int m = 8 * mb + 2 * t + (i & 1);
-          if (m < M) {
-            const int col = 32 * strip + 4 * g + 2 * a + (i >> 1);
-            s_red[(rg * M + m) * T::kNT + col] = acc[a][mb][i];
-          }
-        }
+    write_partials<MB, T::kNT>(acc, s_red, M, strip, rg, g, t);
   }
   __syncthreads();
 
@@ -517,90 +611,36 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
   }
 
   const int nsplit = gridDim.y;
-  auto store = [&](int idx, float v) {
-    const int m = idx / T::kNT;
-    const int n = n0 + (idx - m * T::kNT);
-    if (n < p.N) {
-      if (p.epi == W4_EPI_BIAS) {
-        v += ld_f(p.epi_src, n, p.y_bf16);  // one rounding, like a GEMM's bias epilogue
-      } else if (p.epi == W4_EPI_RESIDUAL) {
-        // out = round(residual + round(y)): the layer output is rounded before
-        // the residual add, as in the reference model's bf16 forward
-        v = ld_f(p.epi_src, (size_t)m * p.N + n, p.y_bf16) + round_to(v, p.y_bf16);
-      }
-      if (pp.world > 0) {  // every rank's buffer of this parity (NVLink stores)
-        const size_t at = (size_t)m * pp.n_full + pp.col_off + n;
-        const int par = (int)(s_epoch & 1u);
-        for (int q = 0; q < pp.world; ++q) {
-          if (p.y_bf16)
-            static_cast<__nv_bfloat16*>(pp.y[par][q])[at] = __float2bfloat16_rn(v);
-          else
-            static_cast<__half*>(pp.y[par][q])[at] = __float2half_rn(v);
-        }
-      } else if (p.y_bf16) {
-        static_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.N + n] = __float2bfloat16_rn(v);
-      } else {
-        static_cast<__half*>(p.y)[(size_t)m * p.N + n] = __float2half_rn(v);
-      }
-    }
-  };
-
   if (nsplit == 1) {
     __syncthreads();
-    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) store(idx, s_red[idx]);
+    const unsigned epoch = s_epoch;
+    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads)
+      store_out(p, pp, epoch, idx / T::kNT, n0 + idx % T::kNT, s_red[idx]);
   } else {
     // Split-K over the cluster: every CTA sums a share of the tile over all
     // ranks' partials in rank order (DSMEM reads), then writes it.
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
+    const unsigned epoch = s_epoch;
     const int rank = (int)cluster.block_rank();
     for (int idx = rank * T::kThreads + threadIdx.x; idx < tile_elems;
          idx += T::kThreads * nsplit) {
       float v = 0.f;
       for (int r = 0; r < nsplit; ++r) v += cluster.map_shared_rank(s_red, r)[idx];
-      store(idx, v);
+      store_out(p, pp, epoch, idx / T::kNT, n0 + idx % T::kNT, v);
     }
     cluster.sync();  // keep this CTA's shared memory alive for the readers
   }
 
   if (pp.world > 0) {
-    // Gathered output: the CTA that finishes last on this rank publishes the
-    // epoch to every rank, then waits until every rank published it here.
-    // Each CTA orders its peer stores before its count at GPU scope (a
-    // cumulative release); the last CTA, having observed every count, makes
-    // all of them visible system-wide with one system-scope fence before it
-    // publishes.
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const unsigned total = gridDim.x * gridDim.y;
-      const unsigned e = s_epoch;
-      if (atomicAdd(&pp.state[1], 1u) == total - 1) {
-        __threadfence_system();
-        for (int q = 0; q < pp.world; ++q) st_release_sys(pp.flags[q] + pp.rank, e);
-        const unsigned* mine = pp.flags[pp.rank];
-        for (int q = 0; q < pp.world; ++q) {
-          const unsigned long long t0 = globaltimer_ns();
-          while ((int)(ld_acquire_sys(mine + q) - e) < 0) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-              report_error(p.err, kErrPeerWait);
-              break;
-            }
-          }
-        }
-        pp.state[1] = 0u;
-        pp.state[0] = e;
-        __threadfence();
-      }
-    }
+    publish_gathered(p, pp, s_epoch, gridDim.x * gridDim.y);
   }
 }
 
 // ---------------------------------------------------------------- host side
 
 namespace {
-
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemvParams, PeerParams);
 
 template <bool B, int MB, int SW, int RG>
 void* kptr() {

@@ -245,8 +245,7 @@ class W4DecodeModel:
             out = {}
             for name, (K, N) in shapes.items():
                 c = tuned_config(1, K, N, bf, bf, None, None, self.device)
-                out[name] = _lib.GemvConfig(c.strips, c.row_groups, c.stages, c.split,
-                                            1 if self.pdl else 0)
+                out[name] = c.with_pdl(1 if self.pdl else 0)
             self._cfgs = out
         return self._cfgs
 

@@ -225,7 +225,7 @@ def w4_matmul(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
         cfg = config or tuned_config(M, K, N, x2.dtype, y_dtype, split_k, num_warps,
                                      packed.device)
         if pdl and not cfg.pdl:
-            cfg = GemvConfig(cfg.strips, cfg.row_groups, cfg.stages, cfg.split, 1)
+            cfg = cfg.with_pdl(1)
         gemv_launch(x2, packed, scales, y, cfg)
     if out is not None:
         return out

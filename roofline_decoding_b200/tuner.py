@@ -70,7 +70,7 @@ def time_config(x2, pool, y, cfg: GemvConfig, reps: int = 3) -> float:
     """
     from .kernels import gemv_launch
 
-    c = GemvConfig(cfg.strips, cfg.row_groups, cfg.stages, cfg.split, 1)
+    c = cfg.with_pdl(1)
     stream = torch.cuda.Stream(x2.device)
     with torch.cuda.stream(stream):
         gemv_launch(x2, *pool[0], y, c)  # validates the config before capture
