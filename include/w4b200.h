@@ -144,6 +144,25 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed,
 int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scales,
             void* y, int y_dtype, int M, int K, int N, void* stream);
 
+/* Calibrated int4 packing (GPTQ), the step the reference lists after its
+ * round-to-nearest packer (devto_article.md:71), in the same packed format
+ * (kernels.py:24-47). One call quantises one 128-row block of W [K, N]
+ * (K = in-features; the block is one scale group):
+ *   w      fp32 [128, N], the block's rows after the error feedback of the
+ *          earlier blocks (read only);
+ *   hinv   fp32 [128, 128] row-major, the block's diagonal block of U, the
+ *          upper Cholesky factor of the conditioned inverse Hessian
+ *          (H^-1 = U^T U, H = X^T X over calibration inputs);
+ *   packed int32 [16, N], the block's 16 packed rows;
+ *   scales fp16 [N], the block's scale row: fp16(max|w| / 7) over the
+ *          error-compensated rows, as the reference packer computes it;
+ *   err    fp32 [128, N], (w_i - dequant(q_i)) / U_ii per row, for the host's
+ *          update of the later rows: W[b1:] -= U[b0:b1, b1:]^T @ err.
+ * Rows are quantised in order; each row's error is fed back into the later
+ * rows of the block. With U diagonal the result is the reference packer's. */
+int w4_gptq_block(const float* w, const float* hinv, int N, int32_t* packed,
+                  void* scales, float* err, void* stream);
+
 /* ---------------------------------------------------------------------
  * Column-parallel GEMV with the all-gather fused into its epilogue.
  *

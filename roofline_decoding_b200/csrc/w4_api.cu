@@ -95,6 +95,7 @@ int init_locked(int device) {
     if (st == W4_OK) st = decode_init_device(di);
     if (st == W4_OK) st = mega_init_device(di);
     if (st == W4_OK) st = gemm_init_device(di);
+    if (st == W4_OK) st = gptq_init_device(di);
   } while (false);
   if (prev != device) cudaSetDevice(prev);
   if (st == W4_OK) {
@@ -261,6 +262,21 @@ int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scale
     return fail(W4_ERR_ALIGNMENT, "w4_gemm: pointers must be 16-byte aligned");
   return launch_gemm(x, x_dtype == W4_BF16, packed, scales, y, y_dtype == W4_BF16, M, K, N,
                      (cudaStream_t)stream);
+}
+
+int w4_gptq_block(const float* w, const float* hinv, int N, int32_t* packed, void* scales,
+                  float* err, void* stream) {
+  if (!w || !hinv || !packed || !scales || !err)
+    return fail(W4_ERR_INVALID_ARG, "w4_gptq_block: null pointer");
+  if (N <= 0) return fail(W4_ERR_INVALID_ARG, "w4_gptq_block: N=%d", N);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(hinv) |
+                      reinterpret_cast<uintptr_t>(packed) | reinterpret_cast<uintptr_t>(err);
+  if ((a & 3u) != 0 || (reinterpret_cast<uintptr_t>(scales) & 1u) != 0)
+    return fail(W4_ERR_ALIGNMENT, "w4_gptq_block: misaligned pointer");
+  int dev = 0;
+  const int st = current_device(&dev);  // initialises the device on first use
+  if (st != W4_OK) return st;
+  return launch_gptq_block(w, hinv, N, packed, scales, err, (cudaStream_t)stream);
 }
 
 size_t w4_peer_flag_bytes(int world) {

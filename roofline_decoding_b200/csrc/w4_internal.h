@@ -70,6 +70,11 @@ int gemm_init_device(const DeviceInfo& di);
 int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
                 int y_bf16, int M, int K, int N, cudaStream_t stream);
 
+// Calibrated (GPTQ) packing, one 128-row block (w4_gptq.cu).
+int gptq_init_device(const DeviceInfo& di);
+int launch_gptq_block(const float* w, const float* u, int N, int32_t* packed, void* scales,
+                      float* err, cudaStream_t stream);
+
 // Whole-step persistent kernel (w4_mega.cu).
 int mega_init_device(const DeviceInfo& di);
 int decode_step_scratch_bytes(const w4_decode_model& m, size_t* bytes);
