@@ -222,7 +222,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     }
   }
   __syncthreads();
-  grid_launch_dependents();
   for (int h = 0; h < G; ++h) sm.q_s[h * kQPitch + tid] = rope_dim(sm.raw + h * kHeadDim, tid, c, s);
   const float kr = rope_dim(sm.raw + G * kHeadDim, tid, c, s);
   const float vv = bf(sm.raw[(G + 1) * kHeadDim + tid]);
@@ -308,6 +307,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 
   // Merge the splits of this KV head over DSMEM, in rank order.
   cluster.sync();
+  // The next kernel (the o projection) may launch now. Triggering here, with
+  // only the merge left, measured fastest for the whole step: earlier, its
+  // CTAs contend with the tile loop; after the merge, its weight prefetch
+  // starts too late.
+  grid_launch_dependents();
   for (int idx = rank * kAttnThreads + tid; idx < G * kHeadDim; idx += kAttnThreads * kAttnSplits) {
     const int h = idx / kHeadDim;
     float M = -INFINITY;
