@@ -528,17 +528,22 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
     hy = [torch.empty((M * world if sharded else M, n), dtype=torch.float16).pin_memory()
           for (M, K, N, dt), n in zip(cases, n_loc)]
     slots = len(pool)
+    # device buffers reused every step, as a serving loop would hold them
+    xd_buf = [torch.empty_like(x) for x in xs]
+    yd_buf = [torch.empty((M, n), dtype=torch.float16, device=device)
+              for (M, K, N, dt), n in zip(cases, n_loc)]
 
     def step(i):
         for k in range(len(cases)):
             p, s = pool[i % slots][k]
-            xd = hx[k].to(device, non_blocking=True)
+            xd = xd_buf[k]
+            xd.copy_(hx[k], non_blocking=True)
             if peers is not None:
                 M, K, N, dt = cases[k]
                 y = peers.gemv(xd, p, s, f"case{k}", N, peers.rank * n_loc[k], config=cfgs[k])
                 hy[k].view(-1).copy_(y.reshape(-1), non_blocking=True)
                 continue
-            y = Kn.w4_matmul(xd, p, s, config=cfgs[k])
+            y = Kn.w4_matmul(xd, p, s, config=cfgs[k], out=yd_buf[k])
             if sharded:
                 import torch.distributed as dist
 
@@ -564,8 +569,8 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
             "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in hx),
             "d2h_bytes_per_step": sum(y.numel() * y.element_size() for y in hy),
             "ms_per_step": round(ms / args.steps, 4),
-            "path": "roofline_decoding_b200.w4_matmul (C ABI w4_gemv_ex) per GEMV, pinned "
-                    "H2D x, D2H y, one host sync per step"}
+            "path": "roofline_decoding_b200.w4_matmul (C ABI w4_gemv_ex) per GEMV into reused "
+                    "device buffers, pinned H2D x, D2H y, one host sync per step"}
 
 
 # ---------------------------------------------------------------- decode workload

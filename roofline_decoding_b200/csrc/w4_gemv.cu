@@ -737,9 +737,40 @@ int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const De
   return gemv_validate_config(M, K, N, c, di);
 }
 
+// An encoded tensor map is a pure function of the arguments below, so the
+// maps of recent launches are kept per host thread and reused when every
+// argument matches (a decode loop launches the same weights every step; an
+// encode costs about a microsecond of host time).
+struct MapKey {
+  const void* base;
+  uint64_t cols, rows;
+  uint32_t box_cols, box_rows;
+  int dt, elem_bytes, swz;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && cols == o.cols && rows == o.rows && box_cols == o.box_cols &&
+           box_rows == o.box_rows && dt == o.dt && elem_bytes == o.elem_bytes && swz == o.swz;
+  }
+};
+struct MapSlot {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapSlots = 64;
+static thread_local MapSlot t_map_cache[kMapSlots];
+
 static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
                      uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
                      CUtensorMapSwizzle swz) {
+  const MapKey key{base, cols, rows, box_cols, box_rows, (int)dt, elem_bytes, (int)swz};
+  const uint64_t h = (reinterpret_cast<uintptr_t>(base) >> 8) ^ (cols * 0x9E3779B1u) ^
+                     (rows << 7) ^ ((uint64_t)box_cols << 17) ^ ((uint64_t)box_rows << 23) ^
+                     ((uint64_t)dt << 29);
+  MapSlot& slot = t_map_cache[(h ^ (h >> 17)) % kMapSlots];
+  if (slot.valid && slot.key == key) {
+    *map = slot.map;
+    return true;
+  }
   EncodeTiledFn enc = encode_tiled_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {cols, rows};
@@ -749,7 +780,11 @@ static bool make_map(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, c
   CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
+  return true;
 }
 
 int gemv_init_device(const DeviceInfo& di) {

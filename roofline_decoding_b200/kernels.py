@@ -13,6 +13,7 @@ library or a GPU is missing.
 """
 from __future__ import annotations
 
+import contextlib
 import json
 import os
 import threading
@@ -38,8 +39,27 @@ _PACK_DTYPE_CODE = {torch.float16: _lib.W4_PACK_F16, torch.bfloat16: _lib.W4_PAC
                     torch.float32: _lib.W4_PACK_F32}
 
 
+def _device_index(device: torch.device) -> int:
+    return torch.cuda.current_device() if device.index is None else device.index
+
+
+try:  # the raw handle of torch's current stream, without building a Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - other torch builds
+    _raw_stream = None
+
+
 def _stream_ptr(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(_device_index(device))
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _on_device(device: torch.device):
+    """torch.cuda.device(device), or nothing when it is already current."""
+    if _device_index(device) == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def _on_cuda(t: torch.Tensor) -> torch.Tensor:
@@ -70,7 +90,7 @@ def pack_weights(w_fp16: torch.Tensor, group_size: int = GROUP_SIZE):
     w = w.contiguous()
     packed = torch.empty((K // 8, N), dtype=torch.int32, device=w.device)
     scales = torch.empty((K // group_size, N), dtype=torch.float16, device=w.device)
-    with torch.cuda.device(w.device):
+    with _on_device(w.device):
         check(_lib.load().w4_pack(w.data_ptr(), _PACK_DTYPE_CODE[w.dtype], packed.data_ptr(),
                                   scales.data_ptr(), K, N, group_size, _stream_ptr(w.device)),
               "pack_weights")
@@ -106,7 +126,7 @@ def dequantize_v1(packed: torch.Tensor, scales: torch.Tensor,
         raise ValueError(f"out_dtype must be float16 or bfloat16, got {out_dtype}")
     packed, scales = packed.contiguous(), scales.contiguous()
     out = torch.empty((K, N), dtype=out_dtype, device=packed.device)
-    with torch.cuda.device(packed.device):
+    with _on_device(packed.device):
         check(_lib.load().w4_dequant(packed.data_ptr(), scales.data_ptr(), out.data_ptr(),
                                      _DTYPE_CODE[out_dtype], K, N, _stream_ptr(packed.device)),
               "dequantize_v1")
@@ -221,7 +241,7 @@ def w4_matmul(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
             raise ValueError("out must be a contiguous tensor of M*N elements of out_dtype")
         y = out
     packed, scales = packed.contiguous(), scales.contiguous()
-    with torch.cuda.device(packed.device):
+    with _on_device(packed.device):
         cfg = config or tuned_config(M, K, N, x2.dtype, y_dtype, split_k, num_warps,
                                      packed.device)
         if pdl and not cfg.pdl:
@@ -307,7 +327,7 @@ def w4_gemm(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
             raise ValueError("out must be a contiguous tensor of M*N elements of out_dtype")
         y = out
     lib = _lib.load()
-    with torch.cuda.device(packed.device):
+    with _on_device(packed.device):
         _lib.check(lib.w4_gemm(x2.data_ptr(), _DTYPE_CODE[x2.dtype], packed.contiguous().data_ptr(),
                                scales.contiguous().data_ptr(), y.data_ptr(), _DTYPE_CODE[y_dtype],
                                M, K, N, _stream_ptr(packed.device)), "w4_gemm")
