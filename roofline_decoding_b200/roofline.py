@@ -7,7 +7,7 @@ bytes are counted from the architecture.
 
 Same API as roofline/roofline.py:23-157 (model dicts, parameter counts,
 bytes per token, measured copy bandwidth, ceilings, % of roofline), plus the
-byte accounting the kernels are judged by: gemv_bytes (one fused GEMV) and
+byte accounting the kernels are measured against: gemv_bytes (one fused GEMV) and
 decode_step_bytes (the W4A16 model actually run: int4 linears, bf16 lm_head).
 """
 from __future__ import annotations

@@ -4,7 +4,7 @@ fp16 activations: the reference's prefill path is dequantize_v1 (fp16
 weights fp16((q - 8) * s)) then an fp32 matmul (scripts/decode_loop.py:51-55);
 the kernel multiplies the same fp16 weights on the tensor cores with fp32
 accumulation, so it matches the oracle's dequantise-then-fp32-matmul up to
-the summation order (tight bar), and the north star's rtol = atol = 1e-2.
+the summation order (tight bar), and within the required rtol = atol = 1e-2.
 bf16 activations use bf16 weights (one rounding of the fp32 product).
 """
 import numpy as np
