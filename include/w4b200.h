@@ -13,8 +13,9 @@
  * Every entry point takes plain device pointers, sizes and a cudaStream_t
  * passed as void*. None of the compute entry points allocates, frees or
  * synchronises, so they can be recorded into a CUDA graph once w4_init()
- * has run on the device. The w4_peer_* memory calls near the end are the
- * exception: they allocate, map and free, and belong outside any capture.
+ * has run on the device. The exceptions, which belong outside any capture:
+ * w4_gemv_tune (a set-up call that allocates and synchronises) and the
+ * w4_peer_* memory calls near the end (they allocate, map and free).
  * All return a w4_status; a non-zero status means nothing was launched.
  */
 #ifndef W4B200_H_
@@ -111,6 +112,20 @@ int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed,
  * when no tuned entry exists. */
 int w4_gemv_default_config(int M, int K, int N, int split_k, int num_warps,
                            w4_gemv_config* out);
+
+/* Replaces roofline/kernels.py:211-247 _tune_num_warps for hosts outside
+ * Python: times the fused GEMV's tile candidates for (M, K, N) on the current
+ * device and writes the fastest to *out (pdl = 0) and, if best_us is not
+ * NULL, its time per launch. Each candidate runs as one CUDA graph of
+ * dependent launches, each on its own copy of random weights, the copies
+ * together exceeding 3x L2, so the time is that of a GEMV in a decode chain
+ * (a lone microsecond launch cannot be timed). split_k / num_warps <= 0 leave
+ * the split / the compute warps free; otherwise they are fixed, as in
+ * w4_gemv. A set-up call: it allocates and frees device memory (up to a few
+ * GB for the largest shapes) and synchronises, so it must not run during
+ * stream capture. */
+int w4_gemv_tune(int M, int K, int N, int x_dtype, int y_dtype, int split_k,
+                 int num_warps, w4_gemv_config* out, float* best_us);
 
 /* Operations fused into the GEMV for a decode step. */
 typedef enum { W4_PRO_NONE = 0, W4_PRO_RMSNORM = 1, W4_PRO_SWIGLU = 2 } w4_prologue;

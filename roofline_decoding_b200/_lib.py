@@ -131,6 +131,8 @@ SIGNATURES = {
                          _c_int, _c_int, _c_void_p]),
     "w4_gptq_block": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p,
                                _c_void_p]),
+    "w4_gemv_tune": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                              ctypes.POINTER(GemvConfig), ctypes.POINTER(ctypes.c_float)]),
     "w4_peer_flag_bytes": (_c_size_t, [_c_int]),
     "w4_gemv_allgather": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int,
                                    _c_int, _c_int, ctypes.POINTER(GemvConfig),

@@ -194,6 +194,22 @@ static int gemv_check(const void* x, int x_dtype, const int32_t* packed, const v
   return W4_OK;
 }
 
+int w4_gemv_tune(int M, int K, int N, int x_dtype, int y_dtype, int split_k, int num_warps,
+                 w4_gemv_config* out, float* best_us) {
+  if (!out) return fail(W4_ERR_INVALID_ARG, "w4_gemv_tune: null out");
+  int st = check_dtype(x_dtype, "w4_gemv_tune x");
+  if (st != W4_OK) return st;
+  if ((st = check_dtype(y_dtype, "w4_gemv_tune y")) != W4_OK) return st;
+  if (M < 1 || M > W4B200_MAX_M || K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_tune: M=%d K=%d N=%d", M, K, N);
+  if (split_k > 16 || split_k > K / 128)
+    return fail(W4_ERR_INVALID_ARG, "split_k=%d must be <= min(16, K/128=%d)", split_k, K / 128);
+  if (num_warps > 0 && num_warps != 4 && num_warps != 8)
+    return fail(W4_ERR_INVALID_ARG, "num_warps=%d must be 4 or 8", num_warps);
+  return gemv_tune(M, K, N, x_dtype == W4_BF16, y_dtype == W4_BF16, split_k, num_warps, out,
+                   best_us);
+}
+
 int w4_gemv_default_config(int M, int K, int N, int split_k, int num_warps,
                            w4_gemv_config* out) {
   if (!out) return fail(W4_ERR_INVALID_ARG, "w4_gemv_default_config: null out");

@@ -47,6 +47,9 @@ int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const D
 int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const DeviceInfo& di,
                        w4_gemv_config* out);
 int launch_gemv(const GemvLaunch& L, cudaStream_t stream);
+// Times the tile candidates for (M, K, N) and returns the fastest (w4_tune.cu).
+int gemv_tune(int M, int K, int N, int x_bf16, int y_bf16, int split_k, int num_warps,
+              w4_gemv_config* out, float* best_us);
 int gemv_init_device(const DeviceInfo& di);
 
 // Decode-step kernels (w4_decode.cu).

@@ -61,6 +61,22 @@ def test_validation_happens_before_any_cuda_call():
     assert st == _lib.W4_ERR_INVALID_ARG
 
 
+def test_tuner_validation_happens_before_any_cuda_call():
+    lib = _lib.load()
+    cfg = _lib.GemvConfig()
+    us = ctypes.c_float(0)
+    for args in ((0, 128, 8, 0, 0, 0, 0),      # M < 1
+                 (17, 128, 8, 0, 0, 0, 0),     # M > 16
+                 (1, 100, 8, 0, 0, 0, 0),      # K % 128
+                 (1, 128, 12, 0, 0, 0, 0),     # N % 8
+                 (1, 128, 8, 2, 0, 0, 0),      # x dtype
+                 (1, 256, 8, 0, 0, 3, 0),      # split_k > K / 128
+                 (1, 128, 8, 0, 0, 0, 6)):     # num_warps
+        assert lib.w4_gemv_tune(*args, ctypes.byref(cfg), ctypes.byref(us)) == \
+            _lib.W4_ERR_INVALID_ARG, args
+    assert lib.w4_gemv_tune(1, 128, 8, 0, 0, 0, 0, None, None) == _lib.W4_ERR_INVALID_ARG
+
+
 def test_decode_step_validation_happens_before_any_cuda_call():
     import ctypes
 

@@ -355,6 +355,27 @@ def test_tuner_picks_a_working_config():
     check_gemv(1536, 1536, config=best)
 
 
+@pytest.mark.parametrize("M,Kd,N,split_k,num_warps", [(1, 1536, 1536, 0, 0), (1, 8960, 1536, 0, 0),
+                                                    (4, 2048, 640, 2, 0), (1, 2048, 1000, 0, 4)])
+def test_native_tuner_picks_a_working_config(M, Kd, N, split_k, num_warps):
+    """w4_gemv_tune (the C-ABI tuner for hosts outside Python)."""
+    import ctypes
+
+    from roofline_decoding_b200 import _lib
+
+    cfg = GemvConfig()
+    us = ctypes.c_float(0)
+    _lib.check(_lib.load().w4_gemv_tune(M, Kd, N, 0, 0, split_k, num_warps, ctypes.byref(cfg),
+                                        ctypes.byref(us)), "w4_gemv_tune")
+    assert 0.5 < us.value < 1000.0
+    assert cfg.pdl == 0 and cfg.strips in (1, 2, 4) and cfg.row_groups in (1, 2, 4, 8)
+    if split_k:
+        assert cfg.split == split_k
+    if num_warps:
+        assert cfg.strips * cfg.row_groups == num_warps
+    check_gemv(Kd, N, M=M, config=cfg, seed=M + N)
+
+
 # ---------------------------------------------------------------- fused GEMV ops
 
 def _bf16_dev(a):
