@@ -601,22 +601,25 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads)
 
   // Row groups -> plane 0, in a fixed order.
   const int tile_elems = M * T::kNT;
-  if (RG > 1) {
+  const int nsplit = gridDim.y;
+  if (nsplit == 1) {
+    // each thread sums its elements' row groups and stores them itself
+    const unsigned epoch = s_epoch;
     for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {
       float v = s_red[idx];
 #pragma unroll
       for (int r = 1; r < RG; ++r) v += s_red[r * tile_elems + idx];
-      s_red[idx] = v;
+      store_out(p, pp, epoch, idx / T::kNT, n0 + idx % T::kNT, v);
     }
-  }
-
-  const int nsplit = gridDim.y;
-  if (nsplit == 1) {
-    __syncthreads();
-    const unsigned epoch = s_epoch;
-    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads)
-      store_out(p, pp, epoch, idx / T::kNT, n0 + idx % T::kNT, s_red[idx]);
   } else {
+    if (RG > 1) {
+      for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {
+        float v = s_red[idx];
+#pragma unroll
+        for (int r = 1; r < RG; ++r) v += s_red[r * tile_elems + idx];
+        s_red[idx] = v;
+      }
+    }
     // Split-K over the cluster: every CTA sums a share of the tile over all
     // ranks' partials in rank order (DSMEM reads), then writes it.
     cg::cluster_group cluster = cg::this_cluster();
@@ -708,19 +711,28 @@ int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const De
   const int groups = K / 128;
   const int sms = di.sm_count > 0 ? di.sm_count : 148;
   const int cw = (num_warps == 4) ? 4 : 8;
-  // Widest tile whose column count does not exceed N (fewer, longer rows of
-  // contiguous 128-byte segments per CTA stream better).
-  int sw = 4;
-  while (sw > 1 && 32 * sw > N) sw /= 2;
-  if (cw / sw > 8) sw = cw / 8;
+  // The widest strips that still leave at least 1.5 column tiles per SM: a
+  // wide tile streams longer row segments, but a grid that does not fill the
+  // GPU costs more (tuned tables: one 32-column strip with 8 row groups wins
+  // on every decode-sized shape, 2-4 strips only once N is large).
+  int sw = 1;
+  for (int c : {4, 2}) {
+    const int t = (N + 32 * c - 1) / (32 * c);
+    if (cw / c >= 1 && 32 * c <= N && 2 * t >= 3 * sms) {
+      sw = c;
+      break;
+    }
+  }
   const int rg = std::max(1, cw / sw);
   const int tiles = (N + 32 * sw - 1) / (32 * sw);
   int split = split_k;
   if (split <= 0) {
-    // Aim for about two CTAs per SM, keep at least RG groups per split.
-    const int want = (2 * sms + tiles - 1) / tiles;
-    split = std::min({want, 8, std::max(1, groups / rg)});
-    split = std::max(split, 1);
+    // Split K only when the column tiles do not fill the GPU: towards about
+    // 2.5 CTAs per SM, keeping at least RG groups per split.
+    split = 1;
+    if (2 * tiles < 3 * sms)
+      split = std::max(1, std::min({(5 * sms + 2 * tiles - 1) / (2 * tiles), 8,
+                                    std::max(1, groups / rg)}));
   }
   w4_gemv_config c{sw, rg, 4, split, 0};
   const int gps = (groups + split - 1) / split;

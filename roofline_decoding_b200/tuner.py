@@ -148,6 +148,7 @@ def main(argv=None) -> None:
     ap.add_argument("--dtypes", default="fp16,bf16")
     ap.add_argument("--quick", action="store_true", help="decode-sweep shapes only")
     args = ap.parse_args(argv)
+    kernels._load_tuned_file()  # keep the shapes this run does not tune in the saved file
     dev = torch.device("cuda", torch.cuda.current_device())
     dts = {"fp16": torch.float16, "bf16": torch.bfloat16}
     shapes = WORKLOAD_SHAPES[:8] if args.quick else WORKLOAD_SHAPES
