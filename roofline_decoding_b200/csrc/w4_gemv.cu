@@ -20,7 +20,8 @@
 // Inner product on the tensor cores (swap-AB): A = W^T tile (16 columns x 16
 // k), B = x^T (16 k x 8 batch rows), D fp32. A thread's 16-byte shared load
 // yields 4 columns x 8 k of one packed row; LOP3 turns each word into four
-// f16x2/bf16x2 pairs of exact (q - 8) values. The k order inside an MMA is a
+// f16x2/bf16x2 pairs of exact small integers, (q - 8) plus a constant that a
+// per-(group, row) correction removes from the sum. The k order inside an MMA is a
 // permutation of the true k order (nibbles (0,4),(1,5) | (2,6),(3,7) of the
 // rows 2t, 2t+1 of each 8-row octet); x is staged in shared memory in the same
 // permuted order, so the sum is unchanged. The per-group scale multiplies the
