@@ -120,6 +120,11 @@ def dist_setup(n_gpus):
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
+        # stdout carries the one JSON line; at NCCL_DEBUG=VERSION (a default of
+        # some images) NCCL prints its version line there, so that level alone
+        # is dropped (debugging levels such as INFO are left as they are)
+        if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
+            del os.environ["NCCL_DEBUG"]
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
