@@ -6,11 +6,23 @@ Workloads (--workload):
          layers and the small model's layers: K x N in 1536x1536 (q/o),
          1536x8960 (gate/up), 8960x1536 (down, tall K), 1536x256 (k/v),
          1024x1024, 1024x2816, each with fp16 and bf16 activations, M = 1.
+         The default line also carries, as sub-records:
+           large           the three Llama-3-70B-like GEMVs on every GPU alone
+                           (per-shape us, GB/s, fraction of HBM);
+           decode          batch-1 greedy decode tok/s of the Qwen2.5-1.5B
+                           architecture (CUDA graph per step), its bytes-moved
+                           roofline, e2e tok/s and a CPU baseline;
+           column_parallel (N > 1 only) the large GEMVs split column-parallel
+                           over the N GPUs with the all-gather fused into the
+                           GEMV (NVLink peer stores), checked bit for bit
+                           against an NCCL all-gather of each rank's slice.
+         --sweep-only leaves the sub-records out.
   gemm   small-batch W4A16 GEMM, K=4096, N=14336, M in {1, 2, 4, 8, 16}.
   large  K=8192,N=28672; K=28672,N=8192; K=8192,N=128256 at M = 1; on N GPUs
-         every rank holds a column slice and an NCCL all-gather assembles y.
+         every rank holds a column slice and the output is all-gathered.
   decode batch-1 greedy decode of a random-init Qwen2.5-1.5B-architecture
          model (int4 linears, bf16 tied lm_head, static KV 2048), tok/s.
+  prefill the tcgen05 W4A16 GEMM at M = 2048 rows, TFLOP/s.
 W ~ N(0, 0.02) fp16 packed to int4 (group 128), x ~ N(0, 1), seeded.
 
 GEMV workloads: one step = every GEMV of the workload once, each on its own
@@ -29,7 +41,8 @@ weights from HBM (the pool exceeds 3x L2).
             and y copied back for every GEMV, one host sync per step.
   cpu_baseline: the reference's dequantise-then-matmul path restated in C
             (oracle/w4_oracle.c, OpenMP) on a bounded sample, rank 0, N = 1.
---impl reference times that CPU restatement as the reference arm.
+--impl reference times that CPU restatement as the reference arm (rank 0
+only; under torchrun the other ranks exit at once, without a process group).
 Multi-GPU: sweep/gemm/decode run as independent replicas (weak scaling, no
 data-path collective); large is column-parallel (strong scaling).
 """
@@ -254,14 +267,24 @@ def cpu_sample(cases_spec, seconds):
     return passes * sum(c[5] for c in cases) / dt / 1e9, passes, dt, c_oracle.max_threads()
 
 
+def workload_config(wl):
+    """The `config` both arms print: the workload itself, nothing about how it runs."""
+    return {"workload": wl["desc"], "batch_rows": sorted({c[0] for c in wl["cases"]}),
+            "gemvs_per_step": len(wl["cases"])}
+
+
 def run_reference(args, rank, world):
-    """--impl reference: the CPU restatement of the reference path, rank 0 only."""
+    """--impl reference: the CPU restatement of the reference path, rank 0 only.
+
+    No process group is made: ranks other than 0 return at once, so that
+    nothing else spins on the host cores while rank 0 uses all of them.
+    """
     if rank != 0:
         return
     from oracle import c_oracle
 
     c_oracle.use_all_cores()  # torchrun sets OMP_NUM_THREADS=1 for every rank
-    wl = WORKLOADS["sweep" if args.workload == "decode" else args.workload]
+    wl = WORKLOADS["sweep" if args.workload in ("decode", "prefill") else args.workload]
     cases = cpu_cases(wl["cases"])
     for _ in range(args.warmup):
         cpu_pass(cases)
@@ -277,7 +300,8 @@ def run_reference(args, rank, world):
         "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (fp32 dequantise-then-matmul)",
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": wl["desc"], "parallelism": "cpu"},
+        "config": workload_config(wl),
+        "parallelism": "cpu (rank 0 only)",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores,
                          "kind": "port",
                          "sample": f"{args.steps} passes over the {len(cases)} GEMVs, one per "
@@ -316,15 +340,21 @@ def build_pool(torch, Kn, cases, device, rank, world, sharded):
     return pool, slots, step_bytes, l2
 
 
-def run_gemv_workload(args, rank, world, local):
+def run_gemv_workload(args, rank, world, local, workload=None, shard=None, cpu=True):
+    """Times one GEMV workload; returns its record on rank 0 (None elsewhere).
+
+    workload defaults to --workload; shard (default: the workload's own
+    setting) splits its GEMVs column-parallel over the ranks; cpu adds the
+    CPU baseline on rank 0 at N = 1.
+    """
     import torch
 
     from roofline_decoding_b200 import kernels as Kn
     from roofline_decoding_b200.roofline import measure_copy_bandwidth_gbs
 
-    wl = WORKLOADS[args.workload]
+    wl = WORKLOADS[workload or args.workload]
     cases = wl["cases"]
-    sharded = wl["sharded"] and world > 1
+    sharded = (wl["sharded"] if shard is None else shard) and world > 1
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peak, peak_kind = measured_peaks()
@@ -374,6 +404,29 @@ def run_gemv_workload(args, rank, world, local):
         for si in range(slots):  # warm every buffer once outside capture
             launch_all(si, pdl=False)
     stream.synchronize()
+
+    gather_check = None
+    if peers is not None:
+        # the fused gather against an NCCL all-gather of every rank's own
+        # slice, computed by the plain GEMV with the same tile: bit for bit
+        import torch.distributed as dist
+
+        ok = True
+        for i, (M, K, N, dt) in enumerate(cases):
+            p, s = pool[0][i]
+            y_peer = peers.gemv(xs[i], p, s, f"case{i}", N, rank * n_loc[i],
+                                config=cfgs[i]).clone()
+            y_loc = Kn.w4_matmul(xs[i], p, s, config=cfgs[i])
+            buf = torch.empty((world * M, n_loc[i]), dtype=y_loc.dtype, device=device)
+            dist.all_gather_into_tensor(buf, y_loc.contiguous())
+            want = buf.view(world, M, n_loc[i]).permute(1, 0, 2).reshape(M, N)
+            ok &= bool(torch.equal(y_peer, want))
+        torch.cuda.synchronize()
+        err = Kn.device_error(local)
+        flags = max_over_ranks([0.0 if ok else 1.0, float(err != 0)], world)
+        gather_check = {"bit_exact": flags[0] == 0.0, "device_error": flags[1] != 0.0,
+                        "against": "NCCL all-gather of each rank's w4_matmul of its slice "
+                                   "(same tile), every GEMV of the workload"}
 
     def capture(si, pdl, ev, gather=True):
         g = torch.cuda.CUDAGraph()
@@ -441,13 +494,15 @@ def run_gemv_workload(args, rank, world, local):
     e2e = run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered,
                   n_loc, peers)
     clk = clocks.summary()
+    line = None
     if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
+        cpu_rec = None
+        if world == 1 and cpu and not args.no_cpu_baseline:
             v, passes, dt_s, cores = cpu_sample(cases, args.cpu_seconds)
-            cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                   "sample": f"{passes} passes over the {len(cases)} GEMVs in {dt_s:.1f} s of "
-                             "oracle/w4_oracle.c dequantise-to-fp16 then fp32 GEMV, OpenMP"}
+            cpu_rec = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                       "sample": f"{passes} passes over the {len(cases)} GEMVs in {dt_s:.1f} s "
+                                 "of oracle/w4_oracle.c dequantise-to-fp16 then fp32 GEMV, "
+                                 "OpenMP"}
         line = {
             "metric": wl["metric"], "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -455,19 +510,18 @@ def run_gemv_workload(args, rank, world, local):
             "scaling": "strong" if sharded else "weak", "vs_baseline": None,
             "dtype": "w4a16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,0.02) weights packed to int4, N(0,1) activations)",
-            "config": {"workload": wl["desc"], "global_batch": 1 if sharded else world,
-                       "parallelism": ((f"column-parallel{world} + all-gather fused into the "
-                                        "GEMV epilogue (NVLink peer stores)" if peers is not None
-                                        else f"column-parallel{world} + NCCL all-gather")
-                                       if sharded else f"replicas{world}"),
-                       "l2": (f"rotating packed-weight pool of {slots} step copies "
-                              f"({slots * step_bytes / 2**20:.0f} MiB >= 3x L2 "
-                              f"{l2 / 2**20:.0f} MiB)"),
-                       "timing": "value: CUDA graph per rotation slot, GEMVs chained with "
-                                 "programmatic dependent launch, events around the steps, "
-                                 "max over ranks; per_case/roofline: per GEMV, a CUDA graph "
-                                 "of PDL-chained launches of that GEMV alone, each on its own "
-                                 "weight copy (copies exceed 3x L2), events around the chain"},
+            "config": workload_config(wl),
+            "parallelism": ((f"column-parallel{world} + all-gather fused into the GEMV "
+                             "epilogue (NVLink peer stores)" if peers is not None
+                             else f"column-parallel{world} + NCCL all-gather")
+                            if sharded else f"replicas{world}"),
+            "l2": (f"rotating packed-weight pool of {slots} step copies "
+                   f"({slots * step_bytes / 2**20:.0f} MiB >= 3x L2 {l2 / 2**20:.0f} MiB)"),
+            "timing": "value: CUDA graph per rotation slot, GEMVs chained with programmatic "
+                      "dependent launch, events around the steps, max over ranks; "
+                      "per_case/roofline: per GEMV, a CUDA graph of PDL-chained launches of "
+                      "that GEMV alone, each on its own weight copy (copies exceed 3x L2), "
+                      "events around the chain",
             "gpu_launches": n_launch * args.steps,
             "roofline": {"bound": "hbm",
                          "kernel": f"w4_gemv_kernel M={dM} K={dK} N={n_loc[dom]} act={ddt}",
@@ -483,16 +537,19 @@ def run_gemv_workload(args, rank, world, local):
             "per_case": per_case,
             "measured_copy_gbs": round(copy_gbs, 1),
             "e2e": e2e,
-            "cpu_baseline": cpu,
+            "cpu_baseline": cpu_rec,
             "clocks": clk,
         }
         if sharded:
             line["gemv_only_ms_per_step"] = round(ms_gemv / args.steps, 4)
             line["gather_ms_per_step"] = round((elapsed_ms - ms_gemv) / args.steps, 4)
-        print(json.dumps(line), flush=True)
+            line["gather_check"] = gather_check
     del graphs_pdl, graphs_gemv  # graphs holding NCCL calls go first
     if peers is not None:
         peers.close()
+    del pool
+    torch.cuda.empty_cache()
+    return line
 
 
 def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
@@ -702,7 +759,7 @@ def run_prefill(args, rank, world, local):
     e_ms = max_over_ranks([c.elapsed_time(d)], world)[0]
     clk = clocks.summary()
     if rank != 0:
-        return
+        return None
     dom = max(range(len(per)), key=lambda i: per[i])
     tot_flops = sum(flops)
     line = {
@@ -735,10 +792,44 @@ def run_prefill(args, rank, world, local):
         "cpu_baseline": None,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
-def run_decode(args, rank, world, local):
+DECODE_PROMPT = 32   # random prompt ids, as the decode configuration states
+DECODE_TOKENS = 256  # greedy tokens timed per run
+
+
+def decode_cpu_baseline(model, prompt, seconds):
+    """tok/s of the same model stepped on the host cores (oracle/decode_oracle.py).
+
+    The reference's decode caller (scripts/decode_loop.py:107-124) restated in
+    fp32 torch with every int4 linear on the reference's dequantise-then-matmul
+    path in C; one warm-up token, then whole tokens for about `seconds`.
+    """
+    from oracle.decode_oracle import DecodeOracle
+
+    ref = DecodeOracle(model)
+    tok = int(prompt[0])
+    ref.step(tok)  # warm the OpenMP pool and the pages
+    n, t0 = 0, time.perf_counter()
+    while n < 2 or (time.perf_counter() - t0 < seconds and n < 64):
+        tok = int(torch_argmax(ref.step(tok)))
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tok/s", "cores": ref.cores, "kind": "port",
+            "sample": f"{n} greedy tokens at positions 1..{n} in {dt:.1f} s: fp32 torch "
+                      "Qwen2.5-1.5B-architecture step on the host, every int4 linear "
+                      "dequantised to fp16 then fp32 GEMV (oracle/w4_oracle.c, OpenMP)"}
+
+
+def torch_argmax(v):
+    import torch
+
+    return torch.argmax(v).item()
+
+
+def run_decode(args, rank, world, local, cpu=True):
+    """Batch-1 greedy decode of the Qwen2.5-1.5B architecture; record on rank 0."""
     import torch
 
     from roofline_decoding_b200.decode import W4DecodeModel
@@ -748,42 +839,44 @@ def run_decode(args, rank, world, local):
     peak, peak_kind = measured_peaks()
     model = W4DecodeModel(device=device, seed=0, mode=args.decode_mode)
     model.capture()
-    prompt_len = 32
     g = torch.Generator().manual_seed(0)
-    prompt = torch.randint(0, model.cfg.vocab, (prompt_len,), generator=g)
-    if prompt_len + args.warmup + args.steps > model.cfg.max_seq:
-        raise SystemExit("prompt + warmup + steps exceed the 2048-token KV cache")
-    model.set_prompt(prompt)
-    for _ in range(prompt_len + args.warmup):
-        model.graph.replay()
+    prompt = torch.randint(0, model.cfg.vocab, (DECODE_PROMPT,), generator=g)
+    steps = DECODE_TOKENS
+    if DECODE_PROMPT + args.warmup + steps > model.cfg.max_seq:
+        raise SystemExit("prompt + warmup + tokens exceed the 2048-token KV cache")
+
+    def prefill():
+        model.set_prompt(prompt)
+        for _ in range(DECODE_PROMPT + args.warmup):  # untimed: prompt, then warm-up tokens
+            model.graph.replay()
+
+    prefill()
     torch.cuda.synchronize()
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         s_ev.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             model.graph.replay()
         e_ev.record()
         torch.cuda.synchronize()
     ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
-    tok_s = world * args.steps / (ms / 1e3)
+    tok_s = world * steps / (ms / 1e3)
     # the attention reads positions 0..pos: bytes at the mean position of the timed steps
-    mean_seq = prompt_len + args.warmup + (args.steps + 1) // 2
+    mean_seq = DECODE_PROMPT + args.warmup + (steps + 1) // 2
     step_bytes = model.bytes_per_step(seq_len=mean_seq)
-    achieved = step_bytes * (args.steps / (ms / 1e3)) / 1e9
+    achieved = step_bytes * (steps / (ms / 1e3)) / 1e9
 
     # e2e: a host-driven loop that reads every token (like .item() per token)
     # and writes it back as the next step's input
     host_tok = torch.zeros((1,), dtype=torch.long).pin_memory()
-    model.set_prompt(prompt)
-    for _ in range(prompt_len + args.warmup):
-        model.graph.replay()
+    prefill()
     host_tok.copy_(model.token)
     torch.cuda.synchronize()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s2.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         model.token.copy_(host_tok, non_blocking=True)
         model.graph.replay()
         host_tok.copy_(model.token, non_blocking=True)
@@ -793,36 +886,71 @@ def run_decode(args, rank, world, local):
     ms2 = max_over_ranks([s2.elapsed_time(e2)], world)[0]
     clk = clocks.summary()
     if rank != 0:
-        return
+        del model
+        torch.cuda.empty_cache()
+        return None
+    cpu_rec = None
+    if cpu and world == 1 and not args.no_cpu_baseline:
+        cpu_rec = decode_cpu_baseline(model, prompt, args.cpu_seconds)
     line = {
         "metric": "batch-1 greedy decode tok/s (W4A16 Qwen2.5-1.5B architecture, CUDA graph)",
-        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "value": round(tok_s, 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "w4a16 linears, bf16 activations/lm_head",
         "data": "synthetic (random-init seeded weights, 32 random prompt ids)",
         "config": {"workload": "Qwen2.5-1.5B architecture decode, 28 layers, hidden 1536, "
                                "int4 linears, tied bf16 lm_head 1536x151936, static KV 2048",
-                   "prompt": prompt_len, "global_batch": world,
-                   "parallelism": f"replicas{world}",
-                   "step": ("one persistent cooperative kernel (w4_decode_step)"
-                            if args.decode_mode == "mega" else
-                            "142 PDL-chained kernels (embed, 5 per layer, lm_head)")},
-        "gpu_launches": model.launches_per_step() * args.steps,
+                   "prompt": DECODE_PROMPT, "tokens": steps},
+        "parallelism": f"replicas{world}",
+        "step": ("one persistent cooperative kernel (w4_decode_step)"
+                 if args.decode_mode == "mega" else
+                 "142 PDL-chained kernels (embed, 5 per layer, lm_head)"),
+        "positions": f"{DECODE_PROMPT + args.warmup}..{DECODE_PROMPT + args.warmup + steps - 1}",
+        "gpu_launches": model.launches_per_step() * steps,
         "roofline": {"bound": "hbm", "kernel": "decode step (all kernels)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": None, "bytes_per_step": step_bytes,
                      "kv_positions_read": mean_seq,
                      "ceiling_tok_s": round(peak * 1e9 / step_bytes, 1)},
-        "e2e": {"value": round(world * args.steps / (ms2 / 1e3), 2), "unit": "tok/s",
+        "e2e": {"value": round(world * steps / (ms2 / 1e3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
-                "ms_per_step": round(ms2 / args.steps, 4),
+                "ms_per_step": round(ms2 / steps, 4),
                 "path": "W4DecodeModel graph replay, token H2D + D2H and a host sync per step"},
-        "cpu_baseline": None,
+        "cpu_baseline": cpu_rec,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    del model
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_default(args, rank, world, local):
+    """The sweep line with the large, decode and (N > 1) column-parallel records."""
+    line = run_gemv_workload(args, rank, world, local, "sweep")
+    if args.sweep_only:
+        return line
+    sub = {"large": run_gemv_workload(args, rank, world, local, "large", shard=False,
+                                      cpu=False)}
+    sub["decode"] = run_decode(args, rank, world, local)
+    if world > 1:
+        sub["column_parallel"] = run_gemv_workload(args, rank, world, local, "large",
+                                                   shard=True, cpu=False)
+    if rank != 0:
+        return None
+    for key in ("large", "column_parallel"):
+        rec = sub.get(key)
+        if rec is not None:  # the sub-records need no second copy of the shared fields
+            for k in ("data", "dtype", "higher_is_better", "vs_baseline", "warmup"):
+                rec.pop(k, None)
+    if sub.get("column_parallel") is not None:
+        one = sub["large"]["ms_per_step"]
+        sub["column_parallel"]["one_gpu_ms_per_step"] = one
+        sub["column_parallel"]["speedup_over_one_gpu"] = round(
+            one / sub["column_parallel"]["ms_per_step"], 3)
+    line.update(sub)
+    return line
 
 
 def main():
@@ -833,6 +961,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep", "gemm", "large", "decode", "prefill"],
                     default="sweep")
+    ap.add_argument("--sweep-only", action="store_true",
+                    help="default workload without the large/decode/column-parallel records")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="large workload on N>1 GPUs: all-gather fused into the GEMV (peer "
@@ -843,16 +973,24 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":  # CPU only: no process group, rank 0 alone works
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world != args.gpus:
+            raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+        run_reference(args, int(os.environ.get("RANK", "0")), world)
+        return
     rank, world, local = dist_setup(args.gpus)
     try:
-        if args.impl == "reference":
-            run_reference(args, rank, world)
-        elif args.workload == "decode":
-            run_decode(args, rank, world, local)
+        if args.workload == "decode":
+            line = run_decode(args, rank, world, local)
         elif args.workload == "prefill":
-            run_prefill(args, rank, world, local)
+            line = run_prefill(args, rank, world, local)
+        elif args.workload == "sweep":
+            line = run_default(args, rank, world, local)
         else:
-            run_gemv_workload(args, rank, world, local)
+            line = run_gemv_workload(args, rank, world, local)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

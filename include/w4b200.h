@@ -222,7 +222,9 @@ int w4_gemv_allgather(const void* x, int x_dtype, const int32_t* packed,
                       void* stream);
 
 /* Device memory another process on this node can map: cudaMalloc plus its
- * IPC handle (W4B200_IPC_HANDLE_BYTES bytes written to handle). */
+ * IPC handle (W4B200_IPC_HANDLE_BYTES bytes written to handle). The memory is
+ * zeroed, and the zeroing has completed on the device, before the handle is
+ * returned (the call synchronises the device). */
 #define W4B200_IPC_HANDLE_BYTES 64
 int w4_peer_alloc(size_t bytes, void** ptr, void* handle);
 int w4_peer_free(void* ptr);
@@ -277,10 +279,16 @@ int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps,
  * library's module, present on every GPU that loads the library until the
  * process exits. It allocates and frees nothing. Its first call on a device
  * looks up that array's address and clears it on the given stream, so make
- * that first call before any stream capture. All calls on a device share the
- * one array: calls that overlap on the GPU race. vocab may not exceed
- * W4B200_STATIC_SCRATCH_MAX_VOCAB (the state keeps a 32-bit row index);
- * other arguments as w4_lm_head_argmax. */
+ * that first call before any stream capture. The address is kept per device
+ * for the life of the process; it does not survive cudaDeviceReset, after
+ * which this entry point must not be called again in the same process. All
+ * calls on a device share the one array: calls that overlap on the GPU race.
+ * The array (W4B200_STATIC_SCRATCH_BYTES) holds the same few words of argmax
+ * state whatever the vocab, so there is no vocab limit beyond a positive int
+ * (W4B200_STATIC_SCRATCH_MAX_VOCAB is that bound, given for information);
+ * hidden is checked against the built sizes before the array is touched.
+ * Other arguments as w4_lm_head_argmax. */
+#define W4B200_STATIC_SCRATCH_BYTES 256
 #define W4B200_STATIC_SCRATCH_MAX_VOCAB 0x7fffffff
 int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
                              const void* embed, int vocab, int hidden,

@@ -338,7 +338,10 @@ int w4_peer_alloc(size_t bytes, void** ptr, void* handle) {
   if (st != W4_OK) return st;
   cudaError_t e = cudaMalloc(ptr, bytes);
   if (e != cudaSuccess) return cuda_fail(e, "w4_peer_alloc cudaMalloc");
+  // The zeroing must have landed before any peer can map the buffer: a peer's
+  // first flag store could otherwise be wiped by a memset still in flight.
   if ((e = cudaMemset(*ptr, 0, bytes)) != cudaSuccess ||
+      (e = cudaDeviceSynchronize()) != cudaSuccess ||
       (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr)) != cudaSuccess) {
     cudaFree(*ptr);
     *ptr = nullptr;
@@ -409,9 +412,10 @@ int w4_lm_head_argmax(const void* h, const void* norm_weight, float eps, const v
   if (workspace_bytes < lm_head_workspace_bytes())
     return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax: workspace of %zu bytes < %zu",
                 workspace_bytes, lm_head_workspace_bytes());
-  if (vocab <= 0 || hidden % 256 != 0 || hidden < 256 || hidden > 2048)
-    return fail(W4_ERR_UNSUPPORTED, "w4_lm_head_argmax: hidden=%d (multiple of 256, <= 2048)",
-                hidden);
+  if (vocab <= 0) return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax: vocab=%d", vocab);
+  if (!lm_head_hidden_supported(hidden))
+    return fail(W4_ERR_UNSUPPORTED,
+                "w4_lm_head_argmax: hidden=%d not in {256, 512, 1024, 1536, 2048}", hidden);
   if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
       (logits && !aligned16(logits)) || !aligned16(workspace))
     return fail(W4_ERR_ALIGNMENT, "w4_lm_head_argmax: pointers must be 16-byte aligned");
@@ -427,14 +431,14 @@ int w4_lm_head_argmax_static(const void* h, const void* norm_weight, float eps,
                              int64_t* token, int64_t* pos, int pdl, void* stream) {
   if (!h || !norm_weight || !embed || !token || !pos)
     return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax_static: null pointer");
-  if (vocab <= 0 || (long long)vocab > (long long)W4B200_STATIC_SCRATCH_MAX_VOCAB)
-    return fail(W4_ERR_INVALID_ARG,
-                "w4_lm_head_argmax_static: vocab=%d outside 1..%lld (the static argmax state "
-                "keeps a 32-bit row index)",
-                vocab, (long long)W4B200_STATIC_SCRATCH_MAX_VOCAB);
-  if (hidden % 256 != 0 || hidden < 256 || hidden > 2048)
+  // the state in the static array is the same few words whatever the vocab:
+  // any positive int vocab fits its 32-bit row index
+  if (vocab <= 0) return fail(W4_ERR_INVALID_ARG, "w4_lm_head_argmax_static: vocab=%d", vocab);
+  // checked before the first call's look-up and clearing of the array
+  if (!lm_head_hidden_supported(hidden))
     return fail(W4_ERR_UNSUPPORTED,
-                "w4_lm_head_argmax_static: hidden=%d (multiple of 256, <= 2048)", hidden);
+                "w4_lm_head_argmax_static: hidden=%d not in {256, 512, 1024, 1536, 2048}",
+                hidden);
   if (!aligned16(h) || !aligned16(norm_weight) || !aligned16(embed) ||
       (logits && !aligned16(logits)))
     return fail(W4_ERR_ALIGNMENT, "w4_lm_head_argmax_static: pointers must be 16-byte aligned");

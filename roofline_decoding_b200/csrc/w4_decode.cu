@@ -615,7 +615,7 @@ int launch_lm_head_argmax(const void* h, const void* norm_w, float eps, const vo
 // started. For them the argmax state of the lm_head kernel lives in a fixed
 // array that the module itself provides. Every call on a device shares that
 // one array, so calls that overlap on the GPU race with each other.
-constexpr size_t kStaticScratchBytes = 256;
+constexpr size_t kStaticScratchBytes = W4B200_STATIC_SCRATCH_BYTES;
 static_assert(sizeof(LmHeadWorkspace) <= kStaticScratchBytes,
               "the lm_head argmax state must fit the static scratch");
 static __device__ __align__(256) unsigned char g_lm_head_scratch[kStaticScratchBytes];

@@ -67,6 +67,10 @@ int lm_head_argmax_static(const void* h, const void* norm_w, float eps, const vo
                           int vocab, int hidden, void* logits, int64_t* token, int64_t* pos,
                           int pdl, cudaStream_t stream);
 int decode_init_device(const DeviceInfo& di);
+// The hidden sizes the lm_head kernel is built for (256, 512, 1024, 1536, 2048).
+inline bool lm_head_hidden_supported(int hidden) {
+  return hidden == 256 || hidden == 512 || hidden == 1024 || hidden == 1536 || hidden == 2048;
+}
 
 // tcgen05 W4A16 GEMM (w4_gemm.cu).
 int gemm_init_device(const DeviceInfo& di);

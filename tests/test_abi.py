@@ -121,3 +121,20 @@ def test_no_cpu_fallback_in_product_path():
     for py in pkg.rglob("*.py"):
         src = py.read_text()
         assert "oracle" not in re.sub(r"#.*", "", src).replace("the oracle", ""), py
+
+
+def test_lm_head_entry_points_reject_unbuilt_hidden_sizes_before_any_cuda_call():
+    """Both argmax entry points accept only the built hidden sizes, and say so
+    before any device work (the static one before it looks up its array)."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)
+    ws_bytes = int(lib.w4_lm_head_workspace_bytes())
+    for hidden in (100, 768, 1280, 1792, 4096):
+        st = lib.w4_lm_head_argmax_static(fake, fake, 1e-6, fake, 1000, hidden, None, fake,
+                                          fake, 0, None)
+        assert st == _lib.W4_ERR_UNSUPPORTED, hidden
+        st = lib.w4_lm_head_argmax(fake, fake, 1e-6, fake, 1000, hidden, None, fake, fake, fake,
+                                   ws_bytes, 0, None)
+        assert st == _lib.W4_ERR_UNSUPPORTED, hidden
+    assert lib.w4_lm_head_argmax_static(fake, fake, 1e-6, fake, 0, 1536, None, fake, fake, 0,
+                                        None) == _lib.W4_ERR_INVALID_ARG
