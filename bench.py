@@ -585,7 +585,12 @@ def chain_time(torch, Kn, x, y, weights, cfg, l2, stream, reps=5):
 
 def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gathered, n_loc,
             peers=None):
-    """Public-API steps: pinned x -> device, fused GEMV(s), y -> pinned host."""
+    """Public-API steps: pinned x -> device, fused GEMV(s), y -> pinned host.
+
+    Unsharded GEMVs go through launch plans (kernels.GemvPlan, C ABI
+    w4_gemv_plan_launch_host): one C call per GEMV enqueues the copy of x, the
+    kernel and the copy of y; one host sync per step.
+    """
     hx = [x.cpu().pin_memory() for x in xs]
     hy = [torch.empty((M * world if sharded else M, n), dtype=torch.float16).pin_memory()
           for (M, K, N, dt), n in zip(cases, n_loc)]
@@ -594,8 +599,21 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
     xd_buf = [torch.empty_like(x) for x in xs]
     yd_buf = [torch.empty((M, n), dtype=torch.float16, device=device)
               for (M, K, N, dt), n in zip(cases, n_loc)]
+    plans = None
+    if not sharded:
+        plans = [[Kn.GemvPlan(p, s, M, xs[k].dtype, torch.float16, config=cfgs[k])
+                  for k, ((p, s), (M, K, N, dt)) in enumerate(zip(pool[si], cases))]
+                 for si in range(slots)]
+        ptrs = [(hx[k].data_ptr(), xd_buf[k].data_ptr(), yd_buf[k].data_ptr(), hy[k].data_ptr())
+                for k in range(len(cases))]
 
     def step(i):
+        if plans is not None:
+            stream = Kn._stream_ptr(device)
+            for plan, (a, b, c, d) in zip(plans[i % slots], ptrs):
+                plan.launch_ptrs(a, b, c, d, stream)
+            torch.cuda.current_stream(device).synchronize()
+            return
         for k in range(len(cases)):
             p, s = pool[i % slots][k]
             xd = xd_buf[k]
@@ -627,12 +645,17 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
     ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
     full = sum(gemv_bytes(M, K, N) for M, K, N, dt in cases)
     bytes_step = full if sharded else full * world
+    if plans is not None:
+        path = ("roofline_decoding_b200.GemvPlan.launch_ptrs (C ABI w4_gemv_plan_launch_host) "
+                "per GEMV: pinned x -> device, GEMV, y -> pinned host in one call; reused device "
+                "buffers; one host sync per step")
+    else:
+        path = ("roofline_decoding_b200 column-parallel GEMV per case with its all-gather, pinned "
+                "H2D x, D2H y, one host sync per step")
     return {"value": round(bytes_step * args.steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in hx),
             "d2h_bytes_per_step": sum(y.numel() * y.element_size() for y in hy),
-            "ms_per_step": round(ms / args.steps, 4),
-            "path": "roofline_decoding_b200.w4_matmul (C ABI w4_gemv_ex) per GEMV into reused "
-                    "device buffers, pinned H2D x, D2H y, one host sync per step"}
+            "ms_per_step": round(ms / args.steps, 4), "path": path}
 
 
 # ---------------------------------------------------------------- decode workload

@@ -107,6 +107,30 @@ int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed,
                const void* scales, void* y, int y_dtype, int M, int K, int N,
                const w4_gemv_config* cfg, void* stream);
 
+/* A GEMV launch prepared once and replayed: tile, kernel instance, encoded
+ * tensor maps and launch geometry for fixed weights, shape and dtypes.
+ * Replaces the per-call work of roofline/kernels.py:250-268 gemv_v3 (tune-
+ * cache lookup, argument set-up, launch) for a loop that calls the same
+ * layer many times: a launch through a plan only binds x, y and the stream.
+ * cfg may be NULL (the w4_gemv_default_config tile). Creating a plan
+ * allocates host memory only; destroy it with w4_gemv_plan_destroy. A plan
+ * belongs to the device that was current when it was made. */
+typedef struct w4_gemv_plan w4_gemv_plan;
+int w4_gemv_plan_create(const int32_t* packed, const void* scales, int M, int K,
+                        int N, int x_dtype, int y_dtype,
+                        const w4_gemv_config* cfg, w4_gemv_plan** plan);
+/* y = x @ dequant(W) with the plan's tile (x, y 16-byte aligned device
+ * pointers of the plan's dtypes). */
+int w4_gemv_plan_launch(const w4_gemv_plan* plan, const void* x, void* y,
+                        void* stream);
+/* The same with host buffers: x_host (M*K elements) is copied into x before
+ * the GEMV and y into y_host (M*N elements) after it, all enqueued on
+ * `stream` (pinned host memory makes the copies asynchronous). x_host or
+ * y_host may be NULL to skip that copy. */
+int w4_gemv_plan_launch_host(const w4_gemv_plan* plan, const void* x_host,
+                             void* x, void* y, void* y_host, void* stream);
+int w4_gemv_plan_destroy(w4_gemv_plan* plan);
+
 /* The configuration w4_gemv would use for (M, K, N, split_k, num_warps).
  * Replaces the choice made by roofline/kernels.py:211-247 _tune_num_warps
  * when no tuned entry exists. */

@@ -6,7 +6,7 @@ reference_gemv, W4Linear, swap_linears, weight_bytes_int4, plus the roofline
 helpers of roofline/roofline.py, and the calibrated (GPTQ) packing the
 reference lists as its next step. Compute goes through libw4b200.so's C ABI.
 """
-from .kernels import (GROUP_SIZE, _TUNE_CACHE, default_config, dequantize_v1, device_error,
+from .kernels import (GROUP_SIZE, _TUNE_CACHE, GemvPlan, default_config, dequantize_v1, device_error,
                       gemv_v2, gemv_v3, pack_weights, reference_gemv, save_tuned_configs,
                       tuned_config, w4_gemm, w4_matmul)
 from .calibrate import accumulate_hessian, calibrate_linears, gptq_pack
@@ -16,7 +16,7 @@ from .roofline import (ORCH_FUSION, QWEN_15B, achieved_bandwidth_percent, ceilin
 
 __version__ = "1.0.0"
 __all__ = [
-    "GROUP_SIZE", "_TUNE_CACHE", "default_config", "dequantize_v1", "device_error", "gemv_v2",
+    "GROUP_SIZE", "_TUNE_CACHE", "GemvPlan", "default_config", "dequantize_v1", "device_error", "gemv_v2",
     "gemv_v3", "pack_weights", "reference_gemv", "save_tuned_configs", "tuned_config",
     "w4_gemm", "w4_matmul", "W4Linear", "swap_linears", "weight_bytes_int4", "ORCH_FUSION", "QWEN_15B",
     "achieved_bandwidth_percent", "ceilings_table", "decode_ceiling", "gemv_bytes",

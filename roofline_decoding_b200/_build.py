@@ -16,7 +16,8 @@ REPO_DIR = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 BUILD_DIR = PKG_DIR / "_build"
 LIB_PATH = PKG_DIR / "libw4b200.so"
-SOURCES = ["w4_api.cu", "w4_pack.cu", "w4_gemv.cu", "w4_decode.cu", "w4_mega.cu",
+SOURCES = ["w4_api.cu", "w4_pack.cu", "w4_gemv.cu", "w4_gemv_ops.cu", "w4_gemv_fused.cu",
+           "w4_decode.cu", "w4_mega.cu",
            "w4_gemm.cu", "w4_gptq.cu", "w4_tune.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

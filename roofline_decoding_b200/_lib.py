@@ -109,6 +109,12 @@ SIGNATURES = {
                             _c_int, _c_int, ctypes.POINTER(GemvConfig), _c_void_p]),
     "w4_gemv_default_config": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int,
                                         ctypes.POINTER(GemvConfig)]),
+    "w4_gemv_plan_create": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                     ctypes.POINTER(GemvConfig), ctypes.POINTER(_c_void_p)]),
+    "w4_gemv_plan_launch": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "w4_gemv_plan_launch_host": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                          _c_void_p]),
+    "w4_gemv_plan_destroy": (_c_int, [_c_void_p]),
     "w4_gemv_fused": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
                                _c_int, _c_int, _c_int, ctypes.POINTER(FusedOps),
                                ctypes.POINTER(GemvConfig), _c_void_p]),

@@ -244,6 +244,46 @@ int w4_gemv_ex(const void* x, int x_dtype, const int32_t* packed, const void* sc
   return launch_gemv(L, (cudaStream_t)stream);
 }
 
+int w4_gemv_plan_create(const int32_t* packed, const void* scales, int M, int K, int N,
+                        int x_dtype, int y_dtype, const w4_gemv_config* cfg,
+                        w4_gemv_plan** plan) {
+  if (!plan) return fail(W4_ERR_INVALID_ARG, "w4_gemv_plan_create: null plan");
+  *plan = nullptr;
+  // x and y are bound at launch: check the rest with stand-in aligned pointers
+  static const int16_t stand_in[8] __attribute__((aligned(16))) = {};
+  int st = gemv_check(stand_in, x_dtype, packed, scales, (void*)stand_in, y_dtype, M, K, N);
+  if (st != W4_OK) return st;
+  w4_gemv_config c;
+  if (cfg) {
+    c = *cfg;
+  } else if ((st = w4_gemv_default_config(M, K, N, 0, 0, &c)) != W4_OK) {
+    return st;
+  }
+  GemvLaunch L{nullptr, packed, scales, nullptr, x_dtype == W4_BF16, y_dtype == W4_BF16,
+               M, K, N, c, {}};
+  void* h = nullptr;
+  if ((st = gemv_plan_create(L, &h)) != W4_OK) return st;
+  *plan = static_cast<w4_gemv_plan*>(h);
+  return W4_OK;
+}
+
+int w4_gemv_plan_launch(const w4_gemv_plan* plan, const void* x, void* y, void* stream) {
+  return w4_gemv_plan_launch_host(plan, nullptr, const_cast<void*>(x), y, nullptr, stream);
+}
+
+int w4_gemv_plan_launch_host(const w4_gemv_plan* plan, const void* x_host, void* x, void* y,
+                             void* y_host, void* stream) {
+  if (!plan || !x || !y) return fail(W4_ERR_INVALID_ARG, "w4_gemv_plan_launch: null argument");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(W4_ERR_ALIGNMENT, "w4_gemv_plan_launch: x and y must be 16-byte aligned");
+  return gemv_plan_launch(plan, x_host, x, y, y_host, (cudaStream_t)stream);
+}
+
+int w4_gemv_plan_destroy(w4_gemv_plan* plan) {
+  gemv_plan_destroy(plan);
+  return W4_OK;
+}
+
 int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void* scales,
                   void* y, int y_dtype, int M, int K, int N, const w4_fused_ops* ops,
                   const w4_gemv_config* cfg, void* stream) {

@@ -76,10 +76,30 @@ int launch_decode_embed(const void* embed, int vocab, int hidden, const int64_t*
 
 // ------------------------------------------------------------------ attention
 
-// Splits of the position range per KV head, one thread-block cluster.
-constexpr int kAttnSplits = 8;
+// Tensor-core flash decoding. The step's q heads of one KV head form the 16
+// rows of an mma.sync m16n8k16 A operand (G <= 16 heads, zero rows above G);
+// K rows of 16 positions are its B operand, so the scores of a 16-position
+// tile are two 16x8 accumulators per 16 dimensions. Those accumulators are,
+// register for register, the A operand of the P.V product (the flash-
+// attention layout), so probabilities never leave registers; V rows are read
+// with transposing ldmatrix. P is split into bf16 hi + lo parts (two MMAs), so
+// P.V keeps about 16 mantissa bits of every probability.
+//
+// Work split: the positions 0..pos of one KV head are cut into S ranges of at
+// most kAttnRows positions (S = ceil(P / kAttnRows), at most kAttnSplits), one
+// CTA each; the 8 warps of a CTA take its 16-position tiles round-robin and
+// merge in shared memory in warp order. Only when S > 1 do the CTAs of the
+// cluster merge over DSMEM in rank order; up to kAttnRows positions one CTA
+// per KV head does everything and no cluster barrier is run. The cached rows
+// below pos were written by earlier steps, so they are copied into shared
+// memory before the grid-dependency wait.
+constexpr int kAttnSplits = 8;   // CTAs (cluster) per KV head
 constexpr int kHeadDim = 128;
-constexpr int kAttnThreads = 128;  // thread i owns dimension i in the RoPE phase
+constexpr int kAttnWarps = 8;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnRows = 256;       // positions per shared-memory pass of one CTA
+constexpr int kRowBytes = kHeadDim * 2;  // one K or V row, 16 chunks of 16 bytes
+constexpr int kObPitch = kHeadDim + 4;   // floats per row of the warp-merge buffer
 
 struct AttnParams {
   const uint16_t* qkv;  // [heads*hd | kv*hd | kv*hd]
@@ -90,7 +110,7 @@ struct AttnParams {
   uint16_t* v_cache;  // [kv, max_seq, hd]
   uint16_t* out;      // [heads*hd]
   int heads, kv_heads, max_seq, group;  // group = heads / kv_heads
-  float scale;
+  float scale_log2;                     // log2(e) / sqrt(hd)
 };
 
 // RoPE (rotate-half) of dimension d of one head, in the reference model's
@@ -102,230 +122,320 @@ __device__ __forceinline__ float rope_dim(const uint16_t* head, int d, float c, 
   return rbf(rbf(x * c) + rbf(rot * s));
 }
 
-// Positions per shared-memory tile of the split's K/V range.
-constexpr int kAttnTile = 64;
-constexpr int kKPitch = kHeadDim + 2;  // bf16 per K row: +1 word, conflict-free column reads
-constexpr int kQPitch = kHeadDim + 4;  // floats per q row: rows land on different banks
-
-// Shared memory layout (attn_smem_bytes gives its size):
-//   raw   bf16 [(G + 2) * 128]           this token's q (G heads), k, v
-//   q_s   f32  [G][kQPitch]              q after RoPE
-//   kn_s  f32  [128], vn_s f32 [128]     this token's k (after RoPE) and v
-//   kt_s  bf16 [kAttnTile][kKPitch]      K rows of the current tile
-//   vt_s  bf16 [kAttnTile][128]          V rows of the current tile
-//   sc_s  f32  [kAttnTile][G]            scores, then probabilities, of the tile
-//   hm_s, hl_s, ha_s  f32 [G]            running max, sum and rescale factor
-//   pm_s, pl_s f32 [G], po_s f32 [G][128]  this split's partial result
-struct AttnSmem {
-  uint16_t* raw;
-  float* q_s;
-  float* kn_s;
-  float* vn_s;
-  uint16_t* kt_s;
-  uint16_t* vt_s;
-  float* sc_s;
-  float* hm_s;
-  float* hl_s;
-  float* ha_s;
-  float* pm_s;
-  float* pl_s;
-  float* po_s;
-};
-
-__host__ __device__ inline size_t attn_raw_bytes(int G) {
-  return ((size_t)(G + 2) * kHeadDim * 2 + 15) / 16 * 16;
+// Byte offset of 16-byte chunk `chunk` of row `row` in a buffer of 256-byte
+// rows: the chunk index is XOR-ed with the row's low 3 bits, so the 8 rows an
+// ldmatrix reads at one chunk fall on 8 different bank groups.
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return (uint32_t)(row * kRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
-__device__ __forceinline__ AttnSmem attn_layout(unsigned char* base, int G) {
-  AttnSmem m;
-  m.raw = reinterpret_cast<uint16_t*>(base);
-  m.q_s = reinterpret_cast<float*>(base + attn_raw_bytes(G));
-  m.kn_s = m.q_s + G * kQPitch;
-  m.vn_s = m.kn_s + kHeadDim;
-  m.kt_s = reinterpret_cast<uint16_t*>(m.vn_s + kHeadDim);
-  m.vt_s = m.kt_s + kAttnTile * kKPitch;
-  m.sc_s = reinterpret_cast<float*>(m.vt_s + kAttnTile * kHeadDim);
-  m.hm_s = m.sc_s + kAttnTile * G;
-  m.hl_s = m.hm_s + G;
-  m.ha_s = m.hl_s + G;
-  m.pm_s = m.ha_s + G;
-  m.pl_s = m.pm_s + G;
-  m.po_s = m.pl_s + G;
-  return m;
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16_attn(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return (uint32_t)to_bf(lo) | ((uint32_t)to_bf(hi) << 16);
 }
 
+// Shared memory (attn_smem_bytes):
+//   kbuf, vbuf  bf16 [kAttnRows][128], swizzled   K and V rows of the pass
+//               (after the last pass: the warp-merge buffer ob, f32
+//               [kAttnWarps][G][kObPitch], aliases them)
+//   qbuf        bf16 [16][128], swizzled          q after RoPE, rows >= G zero
+//   raw         bf16 [G + 2][128]                 this token's q heads, k, v
+//   kvnew       bf16 [2][128]                     this token's k (after RoPE) and v
+//   cs          f32 [2][128]                      cos and sin of the position
+//   wm, wl      f32 [kAttnWarps][16]              per-warp row max and sum
+//   rm, rl      f32 [16]                          the CTA's row max and sum
+//   cpart       f32 [G][128]                      the CTA's unnormalised output
 static size_t attn_smem_bytes(int G) {
-  const size_t f32 = (size_t)G * kQPitch + 2 * kHeadDim;
-  const size_t tiles = (size_t)kAttnTile * kKPitch * 2 + (size_t)kAttnTile * kHeadDim * 2;
-  const size_t rest = (size_t)kAttnTile * G + 5 * (size_t)G + (size_t)G * kHeadDim;
-  return attn_raw_bytes(G) + f32 * 4 + tiles + rest * 4 + 16;
+  const size_t kv = 2 * (size_t)kAttnRows * kRowBytes;
+  const size_t ob = (size_t)kAttnWarps * G * kObPitch * 4;
+  return std::max(kv, ob) + 16 * kRowBytes + (size_t)(G + 2) * kRowBytes + 2 * kRowBytes +
+         2 * kHeadDim * 4 + (2 * kAttnWarps * 16 + 2 * 16) * 4 + (size_t)G * kHeadDim * 4 + 128;
 }
 
-// Loads cache rows [t0, t1) into the tile (none of them the new position).
-__device__ __forceinline__ void load_tile(const AttnSmem& sm, const uint16_t* kc,
-                                          const uint16_t* vc, int t0, int t1, int tid) {
-  const int n = t1 - t0;
-  for (int i = tid; i < n * 16; i += kAttnThreads) {  // 16 uint4 per row for K and V each
-    const int r = i >> 4, c = i & 15;
-    const uint4 kv = __ldcg(reinterpret_cast<const uint4*>(kc + (size_t)(t0 + r) * kHeadDim) + c);
-    const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(vc + (size_t)(t0 + r) * kHeadDim) + c);
-    // K rows have an odd word pitch: store them word by word
-    uint32_t* kd = reinterpret_cast<uint32_t*>(sm.kt_s + r * kKPitch) + 4 * c;
-    kd[0] = kv.x;
-    kd[1] = kv.y;
-    kd[2] = kv.z;
-    kd[3] = kv.w;
-    *(reinterpret_cast<uint4*>(sm.vt_s + r * kHeadDim) + c) = vv;
-  }
-}
-
-// Flash-decoding over this split's positions in tiles of kAttnTile: scores
-// one thread per (position, head) from shared memory, online softmax per head,
-// P.V one thread per dimension; the splits merge over DSMEM in rank order.
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
-  extern __shared__ __align__(16) unsigned char smem_attn[];
+__global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnParams p) {
+  extern __shared__ __align__(128) unsigned char smem_attn[];
   const int G = p.group;
   const int kvh = blockIdx.x;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
+  const int rank = blockIdx.y;  // the cluster spans the splits of one KV head
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const AttnSmem sm = attn_layout(smem_attn, G);
+  const int g = lane >> 2, t = lane & 3;
 
-  // The position and the cached rows below it were written by earlier steps:
-  // load the first tile before waiting for this step's q/k/v.
+  uint8_t* kbuf = smem_attn;
+  uint8_t* vbuf = kbuf + (size_t)kAttnRows * kRowBytes;
+  float* ob = reinterpret_cast<float*>(smem_attn);  // after the last pass
+  uint8_t* qbuf = smem_attn + std::max((size_t)2 * kAttnRows * kRowBytes,
+                                       (size_t)kAttnWarps * G * kObPitch * 4);
+  uint16_t* raw = reinterpret_cast<uint16_t*>(qbuf + 16 * kRowBytes);
+  uint16_t* kvnew = raw + (G + 2) * kHeadDim;
+  float* cs = reinterpret_cast<float*>(kvnew + 2 * kHeadDim);
+  float* wm = cs + 2 * kHeadDim;
+  float* wl = wm + kAttnWarps * 16;
+  float* rm = wl + kAttnWarps * 16;
+  float* rl = rm + 16;
+  float* cpart = rl + 16;
+  const uint32_t k_s = smem_u32(kbuf), v_s = smem_u32(vbuf), q_s = smem_u32(qbuf);
+
+  // The position and the cached rows below it were written by earlier steps.
   const int64_t raw_pos = *p.pos;
   // a position outside the cache is clamped (wrong output, never a wild store)
   const int pos = raw_pos < 0 ? 0 : (raw_pos >= p.max_seq ? p.max_seq - 1 : (int)raw_pos);
   const int P = pos + 1;
-  const int chunk = (P + kAttnSplits - 1) / kAttnSplits;
+  const int S = min(kAttnSplits, (P + kAttnRows - 1) / kAttnRows);
+  int chunk = (P + S - 1) / S;
+  chunk = (chunk + 15) & ~15;
   const int j0 = min(P, rank * chunk), j1 = min(P, j0 + chunk);
+  if (rank >= S && S == 1) return;  // no merge: the other CTAs have nothing to do
   const uint16_t* kc = p.k_cache + (size_t)kvh * p.max_seq * kHeadDim;
   const uint16_t* vc = p.v_cache + (size_t)kvh * p.max_seq * kHeadDim;
-  load_tile(sm, kc, vc, j0, min(min(j1, j0 + kAttnTile), pos), tid);
-  const float c = bf(p.cos_t[(size_t)pos * kHeadDim + tid]);
-  const float s = bf(p.sin_t[(size_t)pos * kHeadDim + tid]);
-  if (tid < G) {
-    sm.hm_s[tid] = -INFINITY;
-    sm.hl_s[tid] = 0.f;
-  }
 
-  grid_dependency_wait();  // qkv comes from the previous kernel
-  {  // this group's q heads, k and v in one vectorised pass
+  // First pass of cached rows [j0, min(j1, pos)), 16-byte asynchronous copies.
+  {
+    const int r1 = min(min(j1, j0 + kAttnRows), pos);
+    for (int i = tid; i < (r1 - j0) * 16; i += kAttnThreads) {
+      const int r = i >> 4, c = i & 15;
+      cp_async16_attn(k_s + swz(r, c), kc + (size_t)(j0 + r) * kHeadDim + 8 * c);
+      cp_async16_attn(v_s + swz(r, c), vc + (size_t)(j0 + r) * kHeadDim + 8 * c);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  {  // cos (threads 0..127) and sin (128..255) of the position
+    const uint16_t* tab = tid < kHeadDim ? p.cos_t : p.sin_t;
+    cs[tid] = bf(tab[(size_t)pos * kHeadDim + (tid & (kHeadDim - 1))]);
+  }
+  grid_launch_dependents();  // the o projection may start streaming its weights
+
+  grid_dependency_wait();  // q/k/v come from the previous kernel
+  {
     const uint4* q = reinterpret_cast<const uint4*>(p.qkv + (size_t)kvh * G * kHeadDim);
     const uint4* k = reinterpret_cast<const uint4*>(p.qkv + (size_t)(p.heads + kvh) * kHeadDim);
     const uint4* v =
         reinterpret_cast<const uint4*>(p.qkv + (size_t)(p.heads + p.kv_heads + kvh) * kHeadDim);
-    uint4* dst = reinterpret_cast<uint4*>(sm.raw);
+    uint4* dst = reinterpret_cast<uint4*>(raw);
     for (int i = tid; i < (G + 2) * 16; i += kAttnThreads) {
       const int h = i >> 4, cc = i & 15;
       dst[i] = __ldcg((h < G ? q + h * 16 : (h == G ? k : v)) + cc);
     }
   }
   __syncthreads();
-  for (int h = 0; h < G; ++h) sm.q_s[h * kQPitch + tid] = rope_dim(sm.raw + h * kHeadDim, tid, c, s);
-  const float kr = rope_dim(sm.raw + G * kHeadDim, tid, c, s);
-  const float vv = bf(sm.raw[(G + 1) * kHeadDim + tid]);
-  sm.kn_s[tid] = kr;
-  sm.vn_s[tid] = vv;
-  if (pos >= j0 && pos < j1) {  // this split owns the new position: store it
-    const size_t at = ((size_t)kvh * p.max_seq + pos) * kHeadDim + tid;
-    p.k_cache[at] = to_bf(kr);
-    p.v_cache[at] = to_bf(vv);
+  // RoPE over every thread: the q heads into the swizzled A operand, k into
+  // kvnew[0], v copied to kvnew[1]; the CTA that owns the new position also
+  // stores its k and v in the cache. Rows G..15 of the A operand are zero.
+  const bool owner = pos >= j0 && pos < j1;
+  for (int e = tid; e < (G + 2) * kHeadDim; e += kAttnThreads) {
+    const int h = e >> 7, d = e & (kHeadDim - 1);
+    if (h < G) {
+      *reinterpret_cast<uint16_t*>(qbuf + swz(h, d >> 3) + 2 * (d & 7)) =
+          to_bf(rope_dim(raw + h * kHeadDim, d, cs[d], cs[kHeadDim + d]));
+    } else {
+      const uint16_t val = h == G ? to_bf(rope_dim(raw + h * kHeadDim, d, cs[d], cs[kHeadDim + d]))
+                                  : raw[h * kHeadDim + d];
+      kvnew[(h - G) * kHeadDim + d] = val;
+      if (owner) {  // this CTA owns the new position: store it
+        const size_t at = ((size_t)kvh * p.max_seq + pos) * kHeadDim + d;
+        (h == G ? p.k_cache : p.v_cache)[at] = val;
+      }
+    }
   }
+  for (int i = tid; i < (16 - G) * 16; i += kAttnThreads)
+    *reinterpret_cast<uint4*>(qbuf + swz(G + (i >> 4), i & 15)) = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
 
-  float o[16];  // o[h] for dimension tid
+  // q fragments (A operand), one set of 4 registers per 16 dimensions
+  uint32_t qa[8][4];
+  float o[16][4];
 #pragma unroll
-  for (int h = 0; h < 16; ++h) o[h] = 0.f;
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
 
-  for (int t0 = j0; t0 < j1; t0 += kAttnTile) {
-    const int t1 = min(j1, t0 + kAttnTile);
-    if (t0 != j0) {
-      __syncthreads();  // the previous tile is consumed
-      load_tile(sm, kc, vc, t0, min(t1, pos), tid);
+  for (int b0 = j0; b0 < j1; b0 += kAttnRows) {  // passes over this CTA's range
+    const int b1 = min(j1, b0 + kAttnRows);
+    const int n = b1 - b0;
+    if (b0 != j0) {  // later passes (more than kAttnRows positions per CTA)
+      __syncthreads();  // the previous pass is consumed
+      const int r1 = min(b1, pos);
+      for (int i = tid; i < (r1 - b0) * 16; i += kAttnThreads) {
+        const int r = i >> 4, c = i & 15;
+        cp_async16_attn(k_s + swz(r, c), kc + (size_t)(b0 + r) * kHeadDim + 8 * c);
+        cp_async16_attn(v_s + swz(r, c), vc + (size_t)(b0 + r) * kHeadDim + 8 * c);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (tid < 32 && pos >= b0 && pos < b1) {  // the new position's row, 16-byte chunks
+      const int r = pos - b0, c = tid & 15;
+      const uint4 v = reinterpret_cast<const uint4*>(kvnew + (tid >> 4) * kHeadDim)[c];
+      *reinterpret_cast<uint4*>((tid < 16 ? kbuf : vbuf) + swz(r, c)) = v;
+    }
+    // rows past the range up to the tile boundary: zeros (a masked probability
+    // times stale shared memory could otherwise be 0 * NaN)
+    for (int i = tid; i < (((n + 15) & ~15) - n) * 16; i += kAttnThreads) {
+      const int r = n + (i >> 4), c = i & 15;
+      *reinterpret_cast<uint4*>(kbuf + swz(r, c)) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(vbuf + swz(r, c)) = make_uint4(0u, 0u, 0u, 0u);
     }
     __syncthreads();
-    const int n = t1 - t0;
-    for (int pi = tid; pi < n * G; pi += kAttnThreads) {  // scores
-      const int jl = pi / G, h = pi - jl * G;
-      const float* qh = sm.q_s + h * kQPitch;
-      float d = 0.f;
-      if (t0 + jl == pos) {
-        for (int e = 0; e < kHeadDim; ++e) d = fmaf(qh[e], sm.kn_s[e], d);
-      } else {
-        const uint32_t* kw = reinterpret_cast<const uint32_t*>(sm.kt_s + jl * kKPitch);
-#pragma unroll 8
-        for (int w = 0; w < kHeadDim / 2; ++w) {
-          const uint32_t kk = kw[w];
-          d = fmaf(qh[2 * w], bf(kk & 0xffffu), d);
-          d = fmaf(qh[2 * w + 1], bf(kk >> 16), d);
+    if (b0 == j0) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        ldsm_x4(q_s + swz((lane & 7) + ((lane >> 3) & 1) * 8, 2 * ks + (lane >> 4)), qa[ks]);
+    }
+    const int n_tiles = (n + 15) >> 4;
+    for (int tile = warp; tile < n_tiles; tile += kAttnWarps) {
+      const int r0 = tile * 16;
+      // scores S^T[head][position] of 16 positions: two 16x8 accumulators
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t kb[4];
+        ldsm_x4(k_s + swz(r0 + (lane & 7) + ((lane >> 4) & 1) * 8, 2 * ks + ((lane >> 3) & 1)),
+                kb);
+        mma_16816<true>(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[0], kb[1]);
+        mma_16816<true>(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], kb[2], kb[3]);
+      }
+      // scale to log2 units, mask positions past the range
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int col = r0 + 8 * a + 2 * t + (i & 1);
+          s[a][i] = col < n ? s[a][i] * p.scale_log2 : -INFINITY;
         }
+      float t0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+      float t1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+        t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
       }
-      sm.sc_s[pi] = d * p.scale;
-    }
-    __syncthreads();
-    for (int h = warp; h < G; h += kAttnThreads / 32) {  // online softmax per head
-      float mx = -INFINITY;
-      for (int jl = lane; jl < n; jl += 32) mx = fmaxf(mx, sm.sc_s[jl * G + h]);
+      const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);  // finite: a tile holds >= 1 position
+      const float al0 = exp2f(m0 - n0), al1 = exp2f(m1 - n1);  // 0 while m is -inf
+      m0 = n0;
+      m1 = n1;
+      float pr[2][4];
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float m_old = sm.hm_s[h];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int jl = lane; jl < n; jl += 32) {
-        const float pr = __expf(sm.sc_s[jl * G + h] - m_new);
-        sm.sc_s[jl * G + h] = pr;
-        sum += pr;
+      for (int a = 0; a < 2; ++a) {
+        pr[a][0] = exp2f(s[a][0] - n0);
+        pr[a][1] = exp2f(s[a][1] - n0);
+        pr[a][2] = exp2f(s[a][2] - n1);
+        pr[a][3] = exp2f(s[a][3] - n1);
+      }
+      l0 = l0 * al0 + ((pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]));
+      l1 = l1 * al1 + ((pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]));
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= al0;
+        o[j][1] *= al0;
+        o[j][2] *= al1;
+        o[j][3] *= al1;
+      }
+      // P as the A operand (rows = heads, k = the 16 positions), hi + lo
+      uint32_t ph[4], pl[4];
+      const float* src[4] = {&pr[0][0], &pr[0][2], &pr[1][0], &pr[1][2]};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float x0 = src[r][0], x1 = src[r][1];
+        const float h0 = rbf(x0), h1 = rbf(x1);
+        ph[r] = pack_bf16x2(h0, h1);
+        pl[r] = pack_bf16x2(x0 - h0, x1 - h1);
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      if (lane == 0) {
-        const float alpha = (m_old == -INFINITY) ? 0.f : __expf(m_old - m_new);
-        sm.ha_s[h] = alpha;
-        sm.hl_s[h] = sm.hl_s[h] * alpha + sum;
-        sm.hm_s[h] = m_new;
+      for (int jj = 0; jj < 8; ++jj) {  // 16 dimensions per transposing ldmatrix
+        uint32_t vb[4];
+        ldsm_x4_t(v_s + swz(r0 + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * jj + (lane >> 4)), vb);
+        mma_16816<true>(o[2 * jj], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+        mma_16816<true>(o[2 * jj], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+        mma_16816<true>(o[2 * jj + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+        mma_16816<true>(o[2 * jj + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
       }
     }
-    __syncthreads();
-#pragma unroll
-    for (int h = 0; h < 16; ++h)
-      if (h < G) o[h] *= sm.ha_s[h];
-    for (int jl = 0; jl < n; ++jl) {  // P.V, thread tid owns dimension tid
-      const float vj = (t0 + jl == pos) ? sm.vn_s[tid] : bf(sm.vt_s[jl * kHeadDim + tid]);
-#pragma unroll
-      for (int h = 0; h < 16; ++h)
-        if (h < G) o[h] = fmaf(sm.sc_s[jl * G + h], vj, o[h]);
-    }
-  }
-  // this split's partial (an empty split leaves m = -inf, l = 0, o = 0)
-#pragma unroll
-  for (int h = 0; h < 16; ++h)
-    if (h < G) sm.po_s[h * kHeadDim + tid] = o[h];
-  if (tid < G) {
-    sm.pm_s[tid] = sm.hm_s[tid];
-    sm.pl_s[tid] = sm.hl_s[tid];
   }
 
-  // Merge the splits of this KV head over DSMEM, in rank order.
-  cluster.sync();
-  // The next kernel (the o projection) may launch now. Triggering here, with
-  // only the merge left, measured fastest for the whole step: earlier, its
-  // CTAs contend with the tile loop; after the merge, its weight prefetch
-  // starts too late.
-  grid_launch_dependents();
-  for (int idx = rank * kAttnThreads + tid; idx < G * kHeadDim; idx += kAttnThreads * kAttnSplits) {
-    const int h = idx / kHeadDim;
-    float M = -INFINITY;
-    for (int r = 0; r < kAttnSplits; ++r) M = fmaxf(M, cluster.map_shared_rank(sm.pm_s, r)[h]);
-    float L = 0.f, O = 0.f;
-    for (int r = 0; r < kAttnSplits; ++r) {
-      const float mr = cluster.map_shared_rank(sm.pm_s, r)[h];
-      const float w = (mr == -INFINITY) ? 0.f : __expf(mr - M);
-      L = fmaf(w, cluster.map_shared_rank(sm.pl_s, r)[h], L);
-      O = fmaf(w, cluster.map_shared_rank(sm.po_s, r)[idx], O);
-    }
-    p.out[(size_t)(kvh * G + h) * kHeadDim + (idx - h * kHeadDim)] = to_bf(O / L);
+  // ---- merge the warps (fixed warp order)
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
+  if (t == 0) {
+    wm[warp * 16 + g] = m0;
+    wm[warp * 16 + g + 8] = m1;
+    wl[warp * 16 + g] = l0;
+    wl[warp * 16 + g + 8] = l1;
+  }
+  __syncthreads();  // every warp is past its last tile: kbuf/vbuf become ob
+  float M0 = -INFINITY, M1 = -INFINITY;
+  for (int w = 0; w < kAttnWarps; ++w) {
+    M0 = fmaxf(M0, wm[w * 16 + g]);
+    M1 = fmaxf(M1, wm[w * 16 + g + 8]);
+  }
+  if (tid < 16) {
+    float M = -INFINITY, L = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * 16 + tid]);
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float mw = wm[w * 16 + tid];
+      if (mw != -INFINITY) L = fmaf(wl[w * 16 + tid], exp2f(mw - M), L);
+    }
+    rm[tid] = M;
+    rl[tid] = L;
+  }
+  const float f0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+  const float f1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (g < G)
+      *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g) * kObPitch + 8 * j + 2 * t) =
+          make_float2(o[j][0] * f0, o[j][1] * f0);
+    if (g + 8 < G)
+      *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g + 8) * kObPitch + 8 * j + 2 * t) =
+          make_float2(o[j][2] * f1, o[j][3] * f1);
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kHeadDim; e += kAttnThreads) {
+    const int h = e >> 7, d = e & (kHeadDim - 1);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) acc += ob[((size_t)w * G + h) * kObPitch + d];
+    if (S == 1)
+      p.out[(size_t)(kvh * G + h) * kHeadDim + d] = to_bf(acc / rl[h]);
+    else
+      cpart[e] = acc;
+  }
+  if (S == 1) return;
+
+  // ---- merge the CTAs of this KV head over DSMEM (rank order); an idle CTA
+  // (rank >= S) contributes m = -inf, l = 0
+  if (rank >= S && tid < 16) {
+    rm[tid] = -INFINITY;
+    rl[tid] = 0.f;
+  }
+  cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
+  for (int e = rank * kAttnThreads + tid; e < G * kHeadDim; e += kAttnThreads * kAttnSplits) {
+    const int h = e >> 7;
+    float M = -INFINITY;
+    for (int r = 0; r < S; ++r) M = fmaxf(M, cluster.map_shared_rank(rm, r)[h]);
+    float L = 0.f, O = 0.f;
+    for (int r = 0; r < S; ++r) {
+      const float mr = cluster.map_shared_rank(rm, r)[h];
+      const float w = (mr == -INFINITY) ? 0.f : exp2f(mr - M);
+      L = fmaf(w, cluster.map_shared_rank(rl, r)[h], L);
+      O = fmaf(w, cluster.map_shared_rank(cpart, r)[e], O);
+    }
+    p.out[(size_t)(kvh * G + h) * kHeadDim + (e & (kHeadDim - 1))] = to_bf(O / L);
+  }
+  cluster.sync();  // keep this CTA's shared memory alive for the readers
 }
 
 int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_t,
@@ -343,7 +453,7 @@ int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_
   p.kv_heads = kv_heads;
   p.max_seq = max_seq;
   p.group = heads / kv_heads;
-  p.scale = 1.0f / sqrtf((float)kHeadDim);
+  p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
   const size_t smem = attn_smem_bytes(p.group);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)kv_heads, kAttnSplits, 1);

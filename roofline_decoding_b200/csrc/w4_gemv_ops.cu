@@ -1,0 +1,17 @@
+// w4_gemv_ops.cu - generic instances of the fused W4A16 GEMV: prologue,
+// epilogue and gathered (peer) output chosen at run time. Used for every
+// combination without an instance of its own, and for the column-parallel
+// gather.
+#include "w4_gemv_kernel.cuh"
+
+namespace w4 {
+
+void* gemv_kernel_generic(int bf16, int mb, int sw, int rg) {
+  if (bf16)
+    return mb == 1 ? gemv_pick_tile<true, 1, kOpsGeneric>(sw, rg)
+                   : gemv_pick_tile<true, 2, kOpsGeneric>(sw, rg);
+  return mb == 1 ? gemv_pick_tile<false, 1, kOpsGeneric>(sw, rg)
+                 : gemv_pick_tile<false, 2, kOpsGeneric>(sw, rg);
+}
+
+}  // namespace w4

@@ -47,6 +47,11 @@ int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const D
 int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const DeviceInfo& di,
                        w4_gemv_config* out);
 int launch_gemv(const GemvLaunch& L, cudaStream_t stream);
+// Launch plans (w4_gemv_plan_*): a prepared launch kept on the host.
+int gemv_plan_create(const GemvLaunch& L, void** plan);
+int gemv_plan_launch(const void* plan, const void* x_host, void* x, void* y, void* y_host,
+                     cudaStream_t stream);
+void gemv_plan_destroy(void* plan);
 // Times the tile candidates for (M, K, N) and returns the fastest (w4_tune.cu).
 int gemv_tune(int M, int K, int N, int x_bf16, int y_bf16, int split_k, int num_warps,
               w4_gemv_config* out, float* best_us);

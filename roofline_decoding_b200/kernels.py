@@ -14,6 +14,7 @@ library or a GPU is missing.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import json
 import os
 import threading
@@ -250,6 +251,73 @@ def w4_matmul(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
     if out is not None:
         return out
     return y[0] if squeeze else y
+
+
+class GemvPlan:
+    """A prepared W4A16 GEMV launch for fixed weights, rows and dtypes (w4_gemv_plan).
+
+    The reference's gemv_v3 looks up its tune cache, sets up arguments and
+    launches on every call (roofline/kernels.py:250-268). A plan does the
+    look-up and the set-up (tile, kernel instance, encoded tensor maps) once;
+    a call then binds x and y and launches: the cheapest host path for a loop
+    that runs the same layer many times. It keeps references to the weights.
+    """
+
+    def __init__(self, packed: torch.Tensor, scales: torch.Tensor, M: int = 1,
+                 x_dtype: torch.dtype = torch.float16, out_dtype: torch.dtype = torch.float16,
+                 config: GemvConfig | None = None, pdl: bool = False):
+        K, N = _check_packed(packed, scales)
+        if x_dtype not in _DTYPE_CODE or out_dtype not in _DTYPE_CODE:
+            raise ValueError("x_dtype and out_dtype must be float16 or bfloat16")
+        if not 1 <= M <= 16:
+            raise ValueError(f"the fused kernel takes 1..16 rows, got {M}")
+        self.packed, self.scales = packed.contiguous(), scales.contiguous()
+        self.M, self.K, self.N = M, K, N
+        self.x_dtype, self.out_dtype = x_dtype, out_dtype
+        self.device = packed.device
+        lib = _lib.load()
+        handle = ctypes.c_void_p()
+        with _on_device(self.device):
+            cfg = config or tuned_config(M, K, N, x_dtype, out_dtype, None, None, self.device)
+            if pdl and not cfg.pdl:
+                cfg = cfg.with_pdl(1)
+            self.config = cfg
+            check(lib.w4_gemv_plan_create(self.packed.data_ptr(), self.scales.data_ptr(), M, K, N,
+                                          _DTYPE_CODE[x_dtype], _DTYPE_CODE[out_dtype], cfg,
+                                          ctypes.byref(handle)), "w4_gemv_plan_create")
+        self._handle = handle.value
+        self._launch = lib.w4_gemv_plan_launch
+        self._launch_host = lib.w4_gemv_plan_launch_host
+        self._destroy = lib.w4_gemv_plan_destroy
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y = x @ dequant(W); x [M, K] (or [K] when M = 1) on the plan's device."""
+        if x.dtype != self.x_dtype or x.numel() != self.M * self.K or not x.is_contiguous() \
+                or x.device != self.device:
+            raise ValueError(f"x must be a contiguous {self.x_dtype} tensor of {self.M}x{self.K} "
+                             f"elements on {self.device}")
+        if out is None:
+            out = torch.empty((self.M, self.N), dtype=self.out_dtype, device=self.device)
+        elif out.dtype != self.out_dtype or out.numel() != self.M * self.N \
+                or not out.is_contiguous() or out.device != self.device:
+            raise ValueError("out must be a contiguous tensor of M*N elements of out_dtype")
+        check(self._launch(self._handle, x.data_ptr(), out.data_ptr(),
+                           _stream_ptr(self.device)), "w4_gemv_plan_launch")
+        return out
+
+    def launch_ptrs(self, x_host: int | None, x: int, y: int, y_host: int | None,
+                    stream: int) -> None:
+        """One C call on raw addresses: copy x_host -> x (if given), the GEMV into
+        y, copy y -> y_host (if given), all enqueued on `stream`. The caller keeps
+        the buffers alive and sized (M*K and M*N elements)."""
+        check(self._launch_host(self._handle, x_host, x, y, y_host, stream),
+              "w4_gemv_plan_launch_host")
+
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h:
+            self._destroy(h)
+            self._handle = None
 
 
 def fused_launch(x2: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,

@@ -138,3 +138,26 @@ def test_lm_head_entry_points_reject_unbuilt_hidden_sizes_before_any_cuda_call()
         assert st == _lib.W4_ERR_UNSUPPORTED, hidden
     assert lib.w4_lm_head_argmax_static(fake, fake, 1e-6, fake, 0, 1536, None, fake, fake, 0,
                                         None) == _lib.W4_ERR_INVALID_ARG
+
+
+def test_plan_validation_happens_before_any_cuda_call():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)
+    plan = ctypes.c_void_p()
+    assert lib.w4_gemv_plan_create(fake, fake, 1, 128, 8, 0, 0, None, None) == \
+        _lib.W4_ERR_INVALID_ARG
+    for args in ((0, 128, 8, 0, 0),     # M < 1
+                 (17, 128, 8, 0, 0),    # M > 16
+                 (1, 100, 8, 0, 0),     # K % 128
+                 (1, 128, 12, 0, 0),    # N % 8
+                 (1, 128, 8, 2, 0)):    # x dtype
+        assert lib.w4_gemv_plan_create(fake, fake, *args, None, ctypes.byref(plan)) == \
+            _lib.W4_ERR_INVALID_ARG, args
+        assert plan.value is None
+    odd = ctypes.c_void_p((1 << 20) + 4)
+    assert lib.w4_gemv_plan_create(odd, fake, 1, 128, 8, 0, 0, None, ctypes.byref(plan)) == \
+        _lib.W4_ERR_ALIGNMENT
+    assert lib.w4_gemv_plan_launch(None, fake, fake, None) == _lib.W4_ERR_INVALID_ARG
+    assert lib.w4_gemv_plan_launch_host(None, None, fake, fake, None, None) == \
+        _lib.W4_ERR_INVALID_ARG
+    assert lib.w4_gemv_plan_destroy(None) == _lib.W4_OK
