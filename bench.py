@@ -587,9 +587,9 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
             peers=None):
     """Public-API steps: pinned x -> device, fused GEMV(s), y -> pinned host.
 
-    Unsharded GEMVs go through launch plans (kernels.GemvPlan, C ABI
-    w4_gemv_plan_launch_host): one C call per GEMV enqueues the copy of x, the
-    kernel and the copy of y; one host sync per step.
+    Unsharded GEMVs go through a batch of launch plans (kernels.GemvPlan.batch,
+    C ABI w4_gemv_plans_launch_host): one C call per step enqueues one copy of
+    all inputs, the GEMVs and one copy of all outputs; one host sync per step.
     """
     hx = [x.cpu().pin_memory() for x in xs]
     hy = [torch.empty((M * world if sharded else M, n), dtype=torch.float16).pin_memory()
@@ -599,19 +599,24 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
     xd_buf = [torch.empty_like(x) for x in xs]
     yd_buf = [torch.empty((M, n), dtype=torch.float16, device=device)
               for (M, K, N, dt), n in zip(cases, n_loc)]
-    plans = None
+    batches = None
     if not sharded:
-        plans = [[Kn.GemvPlan(p, s, M, xs[k].dtype, torch.float16, config=cfgs[k])
-                  for k, ((p, s), (M, K, N, dt)) in enumerate(zip(pool[si], cases))]
-                 for si in range(slots)]
-        ptrs = [(hx[k].data_ptr(), xd_buf[k].data_ptr(), yd_buf[k].data_ptr(), hy[k].data_ptr())
-                for k in range(len(cases))]
+        # one launch-plan batch per rotation slot: the step's inputs lie back to
+        # back in one pinned buffer, its outputs in another
+        batches = [Kn.GemvPlan.batch([Kn.GemvPlan(p, s, M, xs[k].dtype, torch.float16,
+                                                  config=cfgs[k], pdl=True)
+                                      for k, ((p, s), (M, K, N, dt))
+                                      in enumerate(zip(pool[si], cases))])
+                   for si in range(slots)]
+        hx_all = torch.cat([x.view(torch.int16).reshape(-1) for x in hx]).pin_memory()
+        hy_all = torch.empty((batches[0].y_elems,), dtype=torch.float16).pin_memory()
+        xd_all = torch.empty_like(hx_all, device=device)
+        yd_all = torch.empty_like(hy_all, device=device)
+        ptrs = (hx_all.data_ptr(), xd_all.data_ptr(), yd_all.data_ptr(), hy_all.data_ptr())
 
     def step(i):
-        if plans is not None:
-            stream = Kn._stream_ptr(device)
-            for plan, (a, b, c, d) in zip(plans[i % slots], ptrs):
-                plan.launch_ptrs(a, b, c, d, stream)
+        if batches is not None:
+            batches[i % slots].launch_ptrs(*ptrs, Kn._stream_ptr(device))
             torch.cuda.current_stream(device).synchronize()
             return
         for k in range(len(cases)):
@@ -645,10 +650,11 @@ def run_e2e(torch, Kn, pool, cfgs, cases, xs, args, device, world, sharded, gath
     ms = max_over_ranks([s_ev.elapsed_time(e_ev)], world)[0]
     full = sum(gemv_bytes(M, K, N) for M, K, N, dt in cases)
     bytes_step = full if sharded else full * world
-    if plans is not None:
-        path = ("roofline_decoding_b200.GemvPlan.launch_ptrs (C ABI w4_gemv_plan_launch_host) "
-                "per GEMV: pinned x -> device, GEMV, y -> pinned host in one call; reused device "
-                "buffers; one host sync per step")
+    if batches is not None:
+        path = ("roofline_decoding_b200.GemvPlan.batch(...).launch_ptrs (C ABI "
+                "w4_gemv_plans_launch_host): one call per step copies the 12 inputs from pinned "
+                "host memory, runs the 12 GEMVs (programmatic dependent launch) and copies the "
+                "12 outputs back; reused device buffers; one host sync per step")
     else:
         path = ("roofline_decoding_b200 column-parallel GEMV per case with its all-gather, pinned "
                 "H2D x, D2H y, one host sync per step")

@@ -129,6 +129,15 @@ int w4_gemv_plan_launch(const w4_gemv_plan* plan, const void* x, void* y,
  * y_host may be NULL to skip that copy. */
 int w4_gemv_plan_launch_host(const w4_gemv_plan* plan, const void* x_host,
                              void* x, void* y, void* y_host, void* stream);
+/* Several plans in one call, with host buffers (a decode step's GEMVs that
+ * take their inputs from the host, say). The inputs of every plan lie back to
+ * back in x_host (plan i's M*K elements after plan i-1's) and are copied into
+ * x with one copy; the GEMVs run in order, plan i reading its slice of x and
+ * writing its slice of y (its M*N elements, back to back); y is copied into
+ * y_host with one copy. x_host or y_host may be NULL to skip that copy. */
+int w4_gemv_plans_launch_host(const w4_gemv_plan* const* plans, int n,
+                              const void* x_host, void* x, void* y, void* y_host,
+                              void* stream);
 int w4_gemv_plan_destroy(w4_gemv_plan* plan);
 
 /* The configuration w4_gemv would use for (M, K, N, split_k, num_warps).

@@ -114,6 +114,8 @@ SIGNATURES = {
     "w4_gemv_plan_launch": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "w4_gemv_plan_launch_host": (_c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                           _c_void_p]),
+    "w4_gemv_plans_launch_host": (_c_int, [ctypes.POINTER(_c_void_p), _c_int, _c_void_p,
+                                           _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
     "w4_gemv_plan_destroy": (_c_int, [_c_void_p]),
     "w4_gemv_fused": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int,
                                _c_int, _c_int, _c_int, ctypes.POINTER(FusedOps),

@@ -279,6 +279,18 @@ int w4_gemv_plan_launch_host(const w4_gemv_plan* plan, const void* x_host, void*
   return gemv_plan_launch(plan, x_host, x, y, y_host, (cudaStream_t)stream);
 }
 
+int w4_gemv_plans_launch_host(const w4_gemv_plan* const* plans, int n, const void* x_host,
+                              void* x, void* y, void* y_host, void* stream) {
+  if (!plans || n < 1 || !x || !y)
+    return fail(W4_ERR_INVALID_ARG, "w4_gemv_plans_launch_host: null argument or n < 1");
+  for (int i = 0; i < n; ++i)
+    if (!plans[i]) return fail(W4_ERR_INVALID_ARG, "w4_gemv_plans_launch_host: plan %d null", i);
+  if (!aligned16(x) || !aligned16(y))
+    return fail(W4_ERR_ALIGNMENT, "w4_gemv_plans_launch_host: x and y must be 16-byte aligned");
+  return gemv_plans_launch(reinterpret_cast<const void* const*>(plans), n, x_host, x, y, y_host,
+                           (cudaStream_t)stream);
+}
+
 int w4_gemv_plan_destroy(w4_gemv_plan* plan) {
   gemv_plan_destroy(plan);
   return W4_OK;

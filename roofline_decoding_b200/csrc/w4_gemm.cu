@@ -6,16 +6,19 @@
 // fp16 [K, N] copy of the weights, roofline/kernels.py:77-90) followed by an
 // fp32 matmul (scripts/decode_loop.py:51-55). Here the dequantised tile never
 // leaves shared memory:
-//   TMA warp     : X tiles [128 rows x 64 k] (128B swizzle, the canonical
-//                  K-major layout the MMA reads) and the packed words and
-//                  scales of the 128-column W tile, through a 4-slot ring;
-//   4 dequant warps: each thread expands one column's 64 k into fp16
-//                  (q - 8) * s - bit-identical to dequantize_v1 - and writes
-//                  it K-major, 128B-swizzled, into one of two B buffers;
-//   MMA warp     : one thread issues tcgen05.mma (M = 128, N = 128, K = 16,
-//                  fp32 accumulate in tensor memory), four per 64-k stage,
-//                  and commits to the ring's mbarriers;
-//   epilogue     : the dequant warps read the accumulator with tcgen05.ld
+//   TMA warp     : X tiles [up to 256 rows x 64 k] (128B swizzle, the
+//                  canonical K-major layout the MMA reads) and the packed
+//                  words and scales of the W tile (128 or 256 columns),
+//                  through a 3-slot ring;
+//   8 dequant warps: expand each packed word into 8 fp16 (q - 8) * s values
+//                  - bit-identical to dequantize_v1 - and write them K-major,
+//                  128B-swizzled, into one of three B buffers;
+//   MMA warp     : one thread issues tcgen05.mma (M = 128, N = 128 or 256,
+//                  K = 16, fp32 accumulate in tensor memory), four per 64-k
+//                  stage for each of the tile's one or two 128-row halves
+//                  (both halves share one dequantised B tile), and commits to
+//                  the ring's mbarriers;
+//   epilogue     : the dequant warps read the accumulators with tcgen05.ld
 //                  and store Y (fp16 or bf16).
 // bf16 activations use bf16 weights bf16((q - 8) * s) (one rounding of the
 // fp32 product; the reference has no bf16 path). Every wait is bounded; a

@@ -350,6 +350,38 @@ int gemv_plan_launch(const void* handle, const void* x_host, void* x, void* y, v
   return W4_OK;
 }
 
+int gemv_plans_launch(const void* const* handles, int n, const void* x_host, void* x, void* y,
+                      void* y_host, cudaStream_t stream) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  size_t x_total = 0, y_total = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemvPlan& plan = *static_cast<const GemvPlan*>(handles[i]);
+    if (plan.g.device != dev)
+      return fail(W4_ERR_INVALID_ARG, "w4_gemv_plans: plan %d made on device %d, called on %d",
+                  i, plan.g.device, dev);
+    x_total += plan.x_bytes;
+    y_total += plan.y_bytes;
+  }
+  if (x_host && (e = cudaMemcpyAsync(x, x_host, x_total, cudaMemcpyHostToDevice, stream)) !=
+                    cudaSuccess)
+    return cuda_fail(e, "w4_gemv_plans: copy of x to the device");
+  size_t xo = 0, yo = 0;
+  for (int i = 0; i < n; ++i) {
+    const GemvPlan& plan = *static_cast<const GemvPlan*>(handles[i]);
+    const int st = gemv_launch_prepared(plan.g, static_cast<const char*>(x) + xo,
+                                        static_cast<char*>(y) + yo, stream);
+    if (st != W4_OK) return st;
+    xo += plan.x_bytes;
+    yo += plan.y_bytes;
+  }
+  if (y_host && (e = cudaMemcpyAsync(y_host, y, y_total, cudaMemcpyDeviceToHost, stream)) !=
+                    cudaSuccess)
+    return cuda_fail(e, "w4_gemv_plans: copy of y to the host");
+  return W4_OK;
+}
+
 void gemv_plan_destroy(void* handle) { delete static_cast<GemvPlan*>(handle); }
 
 }  // namespace w4

@@ -51,6 +51,8 @@ int launch_gemv(const GemvLaunch& L, cudaStream_t stream);
 int gemv_plan_create(const GemvLaunch& L, void** plan);
 int gemv_plan_launch(const void* plan, const void* x_host, void* x, void* y, void* y_host,
                      cudaStream_t stream);
+int gemv_plans_launch(const void* const* plans, int n, const void* x_host, void* x, void* y,
+                      void* y_host, cudaStream_t stream);
 void gemv_plan_destroy(void* plan);
 // Times the tile candidates for (M, K, N) and returns the fastest (w4_tune.cu).
 int gemv_tune(int M, int K, int N, int x_bf16, int y_bf16, int split_k, int num_warps,

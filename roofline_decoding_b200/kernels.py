@@ -313,11 +313,40 @@ class GemvPlan:
         check(self._launch_host(self._handle, x_host, x, y, y_host, stream),
               "w4_gemv_plan_launch_host")
 
+    @staticmethod
+    def batch(plans: "list[GemvPlan]") -> "GemvPlanBatch":
+        """The plans run back to back by one call (w4_gemv_plans_launch_host)."""
+        return GemvPlanBatch(plans)
+
     def __del__(self):
         h = getattr(self, "_handle", None)
         if h:
             self._destroy(h)
             self._handle = None
+
+
+class GemvPlanBatch:
+    """Plans run in order by one C call, their inputs and outputs back to back.
+
+    x (host and device) holds every plan's M*K inputs one after another, y
+    every plan's M*N outputs; the call copies x in once, runs the GEMVs and
+    copies y out once. Keeps references to the plans.
+    """
+
+    def __init__(self, plans: list[GemvPlan]):
+        if not plans:
+            raise ValueError("a batch needs at least one plan")
+        self.plans = list(plans)
+        self.x_elems = sum(p.M * p.K for p in self.plans)
+        self.y_elems = sum(p.M * p.N for p in self.plans)
+        self._array = (ctypes.c_void_p * len(self.plans))(*[p._handle for p in self.plans])
+        self._launch = _lib.load().w4_gemv_plans_launch_host
+
+    def launch_ptrs(self, x_host: int | None, x: int, y: int, y_host: int | None,
+                    stream: int) -> None:
+        """Copy x_host -> x (if given), run every plan, copy y -> y_host (if given)."""
+        check(self._launch(self._array, len(self.plans), x_host, x, y, y_host, stream),
+              "w4_gemv_plans_launch_host")
 
 
 def fused_launch(x2: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,

@@ -52,3 +52,31 @@ def test_plan_rejects_wrong_inputs():
         plan(torch.zeros((2, 256), dtype=torch.float16, device=DEV))
     with pytest.raises(ValueError):
         K.GemvPlan(p, s, 17, torch.float16)
+
+
+def test_plan_batch_runs_every_plan_on_its_slices():
+    """GemvPlan.batch: inputs back to back in one host buffer, one copy in, the
+    GEMVs in order, one copy out; each slice equals that plan's own call."""
+    shapes = [(1, 1536, 256, torch.float16), (1, 1024, 2816, torch.bfloat16),
+              (2, 512, 1024, torch.float16)]
+    plans, xs = [], []
+    g = torch.Generator().manual_seed(5)
+    for i, (M, Kd, N, dt) in enumerate(shapes):
+        p, s = K.pack_weights(torch.from_numpy(o.normal_weights(Kd, N, seed=i)).to(DEV))
+        plans.append(K.GemvPlan(p, s, M, dt, torch.float16, pdl=bool(i % 2)))
+        xs.append(torch.randn((M, Kd), generator=g).to(dt))
+    batch = K.GemvPlan.batch(plans)
+    hx = torch.cat([x.view(torch.int16).reshape(-1) for x in xs]).pin_memory()
+    hy = torch.empty((batch.y_elems,), dtype=torch.float16).pin_memory()
+    xd = torch.empty_like(hx, device=DEV)
+    yd = torch.empty_like(hy, device=DEV)
+    for _ in range(2):
+        batch.launch_ptrs(hx.data_ptr(), xd.data_ptr(), yd.data_ptr(), hy.data_ptr(),
+                          K._stream_ptr(xd.device))
+        torch.cuda.synchronize()
+        off = 0
+        for plan, x in zip(plans, xs):
+            want = plan(x.to(DEV)).cpu().reshape(-1)
+            assert torch.equal(hy[off:off + want.numel()], want)
+            off += want.numel()
+    assert K.device_error() == 0
