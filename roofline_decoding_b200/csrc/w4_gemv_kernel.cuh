@@ -290,6 +290,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, i
   const int total = M * rows_slice;
   // b0 is the same for every consumer thread, so all of them run the same
   // trips and every shuffle below has its full warp
+  float inv_one = 0.f;  // 1/rms of the single row when it is summed in one pass
   for (int b0 = 0; b0 < total; b0 += 4 * nct) {
     uint4 v[4], aux[4];
 #pragma unroll
@@ -329,12 +330,12 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, i
       for (int off = 16; off > 0; off >>= 1) acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
       if (lane == 0) s_red[warp] = acc2;
       consumer_bar_sync(nct);
-      if (threadIdx.x == 0) {
-        float tot = 0.f;
-        for (int w = 0; w < kCW; ++w) tot += s_red[w];
-        s_inv[0] = rsqrtf(tot / (float)p.K + p.eps);
-      }
-      consumer_bar_sync(nct);
+      // every thread sums the warps' parts itself, in the same order: one
+      // barrier instead of a second barrier after a single thread's sum
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kCW; ++w) tot += s_red[w];
+      inv_one = rsqrtf(tot / (float)p.K + p.eps);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -347,8 +348,9 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, i
         const int r = idx - m * rows_slice;
         const int krow = g0 * 16 + r;
         if (pro != W4_PRO_NONE && krow < g1 * 16)
-          v[u] = stage_transform<kBF16>(pro, v[u], aux[u],
-                                        pro == W4_PRO_RMSNORM ? s_inv[m] : 0.f);
+          v[u] = stage_transform<kBF16>(
+              pro, v[u], aux[u],
+              pro == W4_PRO_RMSNORM ? (rms_one_pass ? inv_one : s_inv[m]) : 0.f);
         o = permute_row<kBF16>(v[u]);
         *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
         const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
@@ -539,8 +541,17 @@ __device__ __forceinline__ void publish_gathered(const GemvParams& p, const Peer
   }
 }
 
+// Two CTAs per SM bound the registers (about 113 for 288 threads). The down
+// projection's SwiGLU instance runs as a split-K grid of 2.6 CTAs per SM, so
+// it is held to three (72 registers): a grid that does not fit the SMs at
+// once runs in two waves.
+template <int OPS>
+constexpr int gemv_min_blocks() {
+  return OPS == kOpsSwigluResidual ? 3 : 2;
+}
+
 template <bool kBF16, int MB, int SW, int RG, int OPS>
-__global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, 2)
+__global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<OPS>())
     w4_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const GemvParams p,
                    const __grid_constant__ PeerParams pp) {
