@@ -162,14 +162,23 @@ int w4_gemv_tune(int M, int K, int N, int x_dtype, int y_dtype, int split_k,
 
 /* Operations fused into the GEMV for a decode step. */
 typedef enum { W4_PRO_NONE = 0, W4_PRO_RMSNORM = 1, W4_PRO_SWIGLU = 2 } w4_prologue;
-typedef enum { W4_EPI_NONE = 0, W4_EPI_BIAS = 1, W4_EPI_RESIDUAL = 2 } w4_epilogue;
+typedef enum {
+  W4_EPI_NONE = 0,
+  W4_EPI_BIAS = 1,
+  W4_EPI_RESIDUAL = 2,
+  W4_EPI_SWIGLU = 3
+} w4_epilogue;
 typedef struct {
   int prologue;            /* W4_PRO_RMSNORM: x <- rmsnorm(x) * norm_weight;
                               W4_PRO_SWIGLU : x is [M, 2K] gate|up, x <- silu(gate) * up */
   const void* norm_weight; /* RMSNorm weight [K] (x's type), 16-byte aligned */
   float eps;               /* RMSNorm epsilon */
   int epilogue;            /* W4_EPI_BIAS: y <- y + bias[n];
-                              W4_EPI_RESIDUAL: y <- residual + round(y) (may alias y) */
+                              W4_EPI_RESIDUAL: y <- residual + round(y) (may alias y);
+                              W4_EPI_SWIGLU: the columns hold gate and up in alternating
+                              blocks of 32 (gate 0..31, up 0..31, gate 32..63, ...), and
+                              y [M, N/2] <- round(round(silu(round(gate))) * round(up)).
+                              Needs strips = 2 and split = 1; epi_src unused */
   const void* epi_src;     /* bias [N] or residual [M, N] (y's type) */
 } w4_fused_ops;
 

@@ -45,6 +45,11 @@ class DecodeOracle:
             d = {}
             for name in ("qkv", "o", "gu", "down"):
                 p, s = L[name]
+                if name == "gu" and getattr(model, "gu_block", 0):
+                    # the fused step interleaves gate and up columns; columns are
+                    # independent, so the permutation back is exact
+                    p = model.deinterleave_gate_up(p, model.gu_block)
+                    s = model.deinterleave_gate_up(s, model.gu_block)
                 d[name] = (np.ascontiguousarray(p.cpu().numpy()),
                            np.ascontiguousarray(s.cpu().numpy()))
                 max_kn = max(max_kn, p.shape[0] * 8 * p.shape[1])

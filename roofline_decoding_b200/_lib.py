@@ -56,7 +56,7 @@ class GemvConfig(ctypes.Structure):
 
 
 W4_PRO_NONE, W4_PRO_RMSNORM, W4_PRO_SWIGLU = 0, 1, 2
-W4_EPI_NONE, W4_EPI_BIAS, W4_EPI_RESIDUAL = 0, 1, 2
+W4_EPI_NONE, W4_EPI_BIAS, W4_EPI_RESIDUAL, W4_EPI_SWIGLU = 0, 1, 2, 3
 
 
 class FusedOps(ctypes.Structure):

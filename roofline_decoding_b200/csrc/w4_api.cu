@@ -304,13 +304,18 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void*
   if (!cfg || !ops) return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: null config or ops");
   if (ops->prologue < W4_PRO_NONE || ops->prologue > W4_PRO_SWIGLU)
     return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: prologue %d unknown", ops->prologue);
-  if (ops->epilogue < W4_EPI_NONE || ops->epilogue > W4_EPI_RESIDUAL)
+  if (ops->epilogue < W4_EPI_NONE || ops->epilogue > W4_EPI_SWIGLU)
     return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: epilogue %d unknown", ops->epilogue);
+  if (ops->epilogue == W4_EPI_SWIGLU &&
+      (cfg->strips != 2 || cfg->split != 1 || N % 64 != 0 || x_dtype != W4_BF16 || M > 8))
+    return fail(W4_ERR_UNSUPPORTED,
+                "w4_gemv_fused: the SwiGLU epilogue needs strips = 2, split = 1, N %% 64 == 0, "
+                "bf16 x and at most 8 rows");
   if (ops->prologue == W4_PRO_RMSNORM && (!ops->norm_weight || !aligned16(ops->norm_weight)))
     return fail(W4_ERR_ALIGNMENT, "w4_gemv_fused: RMSNorm weight missing or not 16-byte aligned");
   if (ops->prologue != W4_PRO_NONE && x_dtype != y_dtype)
     return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: a prologue needs x and y of one type");
-  if (ops->epilogue != W4_EPI_NONE && !ops->epi_src)
+  if ((ops->epilogue == W4_EPI_BIAS || ops->epilogue == W4_EPI_RESIDUAL) && !ops->epi_src)
     return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: epilogue source missing");
   GemvLaunch L{x, packed, scales, y, x_dtype == W4_BF16, y_dtype == W4_BF16, M, K, N, *cfg,
                *ops};

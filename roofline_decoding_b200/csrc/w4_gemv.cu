@@ -168,7 +168,9 @@ int gemv_init_device(const DeviceInfo& di) {
             if (st != W4_OK) return st;
           }
       for (int ops = kOpsFusedFirst; ops <= kOpsFusedLast; ++ops) {
-        const int st = gemv_kernel_attributes(gemv_kernel_fused(ops, sw, rg), di);
+        void* k = gemv_kernel_fused(ops, sw, rg);
+        if (!k) continue;
+        const int st = gemv_kernel_attributes(k, di);
         if (st != W4_OK) return st;
       }
     }

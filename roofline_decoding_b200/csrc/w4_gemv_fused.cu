@@ -1,7 +1,8 @@
 // w4_gemv_fused.cu - instances of the fused W4A16 GEMV for the operation
 // combinations of a decode step (bf16 activations, up to 8 batch rows):
-// RMSNorm + bias (q|k|v), RMSNorm (gate|up), residual (o), SwiGLU + residual
-// (down). Each contains only its own prologue and epilogue code.
+// RMSNorm + bias (q|k|v), RMSNorm (gate|up), RMSNorm + SwiGLU (gate|up with
+// gate and up interleaved), residual (o), SwiGLU + residual (down). Each
+// contains only its own prologue and epilogue code.
 #include "w4_gemv_kernel.cuh"
 
 namespace w4 {
@@ -12,6 +13,8 @@ void* gemv_kernel_fused(int ops, int sw, int rg) {
     case kOpsRms: return gemv_pick_tile<true, 1, kOpsRms>(sw, rg);
     case kOpsResidual: return gemv_pick_tile<true, 1, kOpsResidual>(sw, rg);
     case kOpsSwigluResidual: return gemv_pick_tile<true, 1, kOpsSwigluResidual>(sw, rg);
+    // the SwiGLU epilogue pairs a gate strip with an up strip: two strips only
+    case kOpsRmsSwiglu: return sw == 2 ? gemv_pick_tile<true, 1, kOpsRmsSwiglu>(sw, rg) : nullptr;
     default: return nullptr;
   }
 }

@@ -95,16 +95,18 @@ enum : int {
   kOpsRms = 3,             // RMSNorm prologue (gate|up)
   kOpsResidual = 4,        // residual epilogue (o)
   kOpsSwigluResidual = 5,  // SwiGLU prologue, residual epilogue (down)
+  kOpsRmsSwiglu = 6,       // RMSNorm prologue, SwiGLU epilogue (gate|up, interleaved)
 };
-constexpr int kOpsFusedFirst = kOpsRmsBias, kOpsFusedLast = kOpsSwigluResidual;
+constexpr int kOpsFusedFirst = kOpsRmsBias, kOpsFusedLast = kOpsRmsSwiglu;
 constexpr int ops_pro(int ops) {
-  return (ops == kOpsRmsBias || ops == kOpsRms) ? W4_PRO_RMSNORM
+  return (ops == kOpsRmsBias || ops == kOpsRms || ops == kOpsRmsSwiglu) ? W4_PRO_RMSNORM
          : ops == kOpsSwigluResidual            ? W4_PRO_SWIGLU
                                                 : W4_PRO_NONE;
 }
 constexpr int ops_epi(int ops) {
   return ops == kOpsRmsBias                                     ? W4_EPI_BIAS
          : (ops == kOpsResidual || ops == kOpsSwigluResidual) ? W4_EPI_RESIDUAL
+         : ops == kOpsRmsSwiglu                                 ? W4_EPI_SWIGLU
                                                                : W4_EPI_NONE;
 }
 // The fused instance for a (prologue, epilogue) pair, or kOpsGeneric.
@@ -114,6 +116,7 @@ constexpr int ops_for(int pro, int epi) {
          : (pro == W4_PRO_RMSNORM && epi == W4_EPI_NONE)    ? kOpsRms
          : (pro == W4_PRO_NONE && epi == W4_EPI_RESIDUAL)   ? kOpsResidual
          : (pro == W4_PRO_SWIGLU && epi == W4_EPI_RESIDUAL) ? kOpsSwigluResidual
+         : (pro == W4_PRO_RMSNORM && epi == W4_EPI_SWIGLU)  ? kOpsRmsSwiglu
                                                             : kOpsGeneric;
 }
 
@@ -717,7 +720,32 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
   __syncthreads();
 
   // Row groups -> plane 0, in a fixed order.
-  if (nsplit == 1) {
+  if (epi == W4_EPI_SWIGLU) {
+    // Two strips: gate columns then the matching up columns (the weights
+    // alternate blocks of 32); y has half the columns. The bf16 arithmetic of
+    // the reference model's MLP: gate and up rounded, silu in fp32 rounded,
+    // the product rounded by the store. Host-checked: SW == 2, no split.
+    constexpr int kHalf = T::kNT / 2;
+    for (int o = threadIdx.x; o < M * kHalf; o += T::kThreads) {
+      const int m = o / kHalf, c = o - m * kHalf;
+      float gv = s_red[m * T::kNT + c], uv = s_red[m * T::kNT + kHalf + c];
+#pragma unroll
+      for (int r = 1; r < RG; ++r) {
+        gv += s_red[(r * M + m) * T::kNT + c];
+        uv += s_red[(r * M + m) * T::kNT + kHalf + c];
+      }
+      const int n = n0 / 2 + c;
+      if (2 * n < p.N) {
+        const float gr = round_to(gv, p.y_bf16), ur = round_to(uv, p.y_bf16);
+        const float a = round_to(gr / (1.0f + __expf(-gr)), p.y_bf16);
+        const size_t at = (size_t)m * (p.N / 2) + n;
+        if (p.y_bf16)
+          static_cast<__nv_bfloat16*>(p.y)[at] = __float2bfloat16_rn(a * ur);
+        else
+          static_cast<__half*>(p.y)[at] = __float2half_rn(a * ur);
+      }
+    }
+  } else if (nsplit == 1) {
     // each thread sums its elements' row groups and stores them itself
     const unsigned epoch = s_epoch;
     for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {

@@ -25,6 +25,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
+from ._lib import GemvConfig
 from .kernels import fused_launch, pack_weights, tuned_config, w4_matmul
 from .roofline import decode_step_bytes
 
@@ -80,6 +81,24 @@ class W4DecodeModel:
     """Static-KV, graph-captured batch-1 greedy decoder with int4 linears."""
 
     MODES = ("mega", "fused", "torch")
+    GU_BLOCK = 32  # gate/up interleave of the fused step (the GEMV strip width)
+
+    @staticmethod
+    def interleave_gate_up(w: torch.Tensor, block: int) -> torch.Tensor:
+        """[..., gate | up] columns -> alternating blocks: gate 0..b-1, up 0..b-1, gate b.."""
+        *lead, n2 = w.shape
+        inter = n2 // 2
+        g = w[..., :inter].reshape(*lead, inter // block, 1, block)
+        u = w[..., inter:].reshape(*lead, inter // block, 1, block)
+        return torch.cat([g, u], dim=-2).reshape(*lead, n2)
+
+    @staticmethod
+    def deinterleave_gate_up(w: torch.Tensor, block: int) -> torch.Tensor:
+        """The inverse of interleave_gate_up: alternating blocks -> [gate | up]."""
+        *lead, n2 = w.shape
+        v = w.reshape(*lead, n2 // (2 * block), 2, block)
+        return torch.cat([v[..., 0, :].reshape(*lead, n2 // 2),
+                          v[..., 1, :].reshape(*lead, n2 // 2)], dim=-1)
 
     def __init__(self, cfg: DecodeConfig = QWEN25_15B, device: str | torch.device = "cuda",
                  seed: int = 0, std: float = 0.02, keep_dense: bool = False, fused: bool = True,
@@ -109,13 +128,19 @@ class W4DecodeModel:
         self.post_norms = torch.empty((nl, h), dtype=bf, device=self.device)
         self.layers = []
         self.dense: list[DenseLayer] | None = [] if keep_dense else None
+        # The fused step computes SwiGLU in the gate|up GEMV's epilogue: there the
+        # gate and up columns alternate in blocks of GU_BLOCK, so that one CTA
+        # holds matching gate and up outputs. Columns are independent, so the
+        # permutation is exact; the other modes keep [gate | up].
+        self.gu_block = self.GU_BLOCK if self.mode == "fused" else 0
         for li in range(nl):
             w_qkv = _rand((h, h + 2 * kv), gen, self.device, std).half()
             w_o = _rand((h, h), gen, self.device, std).half()
             w_gu = _rand((h, 2 * inter), gen, self.device, std).half()
             w_down = _rand((inter, h), gen, self.device, std).half()
             layer = {}
-            for name, w in (("qkv", w_qkv), ("o", w_o), ("gu", w_gu), ("down", w_down)):
+            w_gu_packed = self.interleave_gate_up(w_gu, self.gu_block) if self.gu_block else w_gu
+            for name, w in (("qkv", w_qkv), ("o", w_o), ("gu", w_gu_packed), ("down", w_down)):
                 K = shapes[name][0]
                 pk, sc = pack_weights(w)
                 dp = self.w4[name][0][li * K // 8:(li + 1) * K // 8]
@@ -159,7 +184,9 @@ class W4DecodeModel:
         self.h = torch.zeros((1, h), dtype=bf, device=self.device)
         self.qkv_buf = torch.empty((1, h + 2 * kv), dtype=bf, device=self.device)
         self.attn_buf = torch.empty((1, h), dtype=bf, device=self.device)
-        self.gu_buf = torch.empty((1, 2 * inter), dtype=bf, device=self.device)
+        # the fused step's gate|up GEMV writes silu(gate) * up; the others write gate | up
+        self.gu_buf = torch.empty((1, inter if self.gu_block else 2 * inter), dtype=bf,
+                                  device=self.device)
         self.ws = torch.zeros((int(_lib.load().w4_lm_head_workspace_bytes()),), dtype=torch.uint8,
                               device=self.device)
         self._cfgs: dict | None = None
@@ -245,6 +272,8 @@ class W4DecodeModel:
             out = {}
             for name, (K, N) in shapes.items():
                 c = tuned_config(1, K, N, bf, bf, None, None, self.device)
+                if name == "gu" and self.gu_block and (c.strips != 2 or c.split != 1):
+                    c = GemvConfig(2, 4, 2, 1, 0)  # the SwiGLU epilogue pairs two strips
                 out[name] = c.with_pdl(1 if self.pdl else 0)
             self._cfgs = out
         return self._cfgs
@@ -271,9 +300,11 @@ class W4DecodeModel:
                 "w4_decode_attention")
             fused_launch(self.attn_buf, *L["o"], self.h, cfgs["o"],
                          epilogue=_lib.W4_EPI_RESIDUAL, epi_src=self.h)
+            # gate|up with SwiGLU in its epilogue (interleaved columns), then the
+            # down projection on the activation, residual added in its epilogue
             fused_launch(self.h, *L["gu"], self.gu_buf, cfgs["gu"], _lib.W4_PRO_RMSNORM,
-                         L["post_norm"], cfg.rms_eps)
-            fused_launch(self.gu_buf, *L["down"], self.h, cfgs["down"], _lib.W4_PRO_SWIGLU,
+                         L["post_norm"], cfg.rms_eps, _lib.W4_EPI_SWIGLU)
+            fused_launch(self.gu_buf, *L["down"], self.h, cfgs["down"],
                          epilogue=_lib.W4_EPI_RESIDUAL, epi_src=self.h)
         chk(lib.w4_lm_head_argmax(self.h.data_ptr(), self.final_norm.data_ptr(), cfg.rms_eps,
                                   self.embed.data_ptr(), cfg.vocab, cfg.hidden,

@@ -33,6 +33,9 @@ def reference_logits(model: W4DecodeModel, ids: list[int]) -> list[torch.Tensor]
     f = lambda t: t.detach().float().cpu()  # noqa: E731
     L = [{k: (deq(v) if isinstance(v, tuple) else f(v)) for k, v in layer.items()}
          for layer in model.layers]
+    if model.gu_block:  # the fused step interleaves gate and up columns
+        for W in L:
+            W["gu"] = model.deinterleave_gate_up(W["gu"], model.gu_block)
     embed, fnorm = f(model.embed), f(model.final_norm)
     cos, sin = f(model.cos), f(model.sin)
     kc = [[] for _ in L]
