@@ -82,8 +82,8 @@ int launch_decode_embed(const void* embed, int vocab, int hidden, const int64_t*
 // tile are two 16x8 accumulators per 16 dimensions. Those accumulators are,
 // register for register, the A operand of the P.V product (the flash-
 // attention layout), so probabilities never leave registers; V rows are read
-// with transposing ldmatrix. P is split into bf16 hi + lo parts (two MMAs), so
-// P.V keeps about 16 mantissa bits of every probability.
+// with transposing ldmatrix. P enters P.V rounded to bf16, as in the
+// reference model's bf16 attention; the softmax sums stay in fp32.
 //
 // Work split: the positions 0..pos of one KV head are cut into S ranges of at
 // most kAttnRows positions (S = ceil(P / kAttnRows), at most kAttnSplits), one
@@ -100,6 +100,7 @@ constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kAttnRows = 256;       // positions per shared-memory pass of one CTA
 constexpr int kRowBytes = kHeadDim * 2;  // one K or V row, 16 chunks of 16 bytes
 constexpr int kObPitch = kHeadDim + 4;   // floats per row of the warp-merge buffer
+constexpr int kAttnTilesPerWarp = 1;     // 16-position tiles per warp before another joins
 
 struct AttnParams {
   const uint16_t* qkv;  // [heads*hd | kv*hd | kv*hd]
@@ -259,6 +260,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnPa
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
 
+  // Warps that take tiles: with one pass, about kAttnTilesPerWarp tiles each,
+  // in contiguous runs (a short context needs fewer warps, and with one warp
+  // the cross-warp merge is skipped); with several passes all warps,
+  // round-robin.
+  const bool one_pass = j1 - j0 <= kAttnRows;
+  const int nt_first = (min(j1 - j0, kAttnRows) + 15) >> 4;
+  const int W = one_pass ? max(1, min(kAttnWarps, (nt_first + kAttnTilesPerWarp - 1) /
+                                                      kAttnTilesPerWarp))
+                         : kAttnWarps;
   for (int b0 = j0; b0 < j1; b0 += kAttnRows) {  // passes over this CTA's range
     const int b1 = min(j1, b0 + kAttnRows);
     const int n = b1 - b0;
@@ -292,7 +302,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnPa
         ldsm_x4(q_s + swz((lane & 7) + ((lane >> 3) & 1) * 8, 2 * ks + (lane >> 4)), qa[ks]);
     }
     const int n_tiles = (n + 15) >> 4;
-    for (int tile = warp; tile < n_tiles; tile += kAttnWarps) {
+    const int tpw = (n_tiles + W - 1) / W;
+    const int t_begin = one_pass ? warp * tpw : warp;
+    const int t_end = one_pass ? min(n_tiles, t_begin + tpw) : n_tiles;
+    const int t_step = one_pass ? 1 : kAttnWarps;
+    for (int tile = t_begin; tile < t_end; tile += t_step) {
       const int r0 = tile * 16;
       // scores S^T[head][position] of 16 positions: two 16x8 accumulators
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -340,24 +354,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnPa
         o[j][2] *= al1;
         o[j][3] *= al1;
       }
-      // P as the A operand (rows = heads, k = the 16 positions), hi + lo
-      uint32_t ph[4], pl[4];
+      // P as the A operand (rows = heads, k = the 16 positions), rounded to
+      // bf16 as the reference model's attention does before P.V; the row sums
+      // l stay in fp32
+      uint32_t ph[4];
       const float* src[4] = {&pr[0][0], &pr[0][2], &pr[1][0], &pr[1][2]};
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const float x0 = src[r][0], x1 = src[r][1];
-        const float h0 = rbf(x0), h1 = rbf(x1);
-        ph[r] = pack_bf16x2(h0, h1);
-        pl[r] = pack_bf16x2(x0 - h0, x1 - h1);
-      }
+      for (int r = 0; r < 4; ++r) ph[r] = pack_bf16x2(src[r][0], src[r][1]);
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj) {  // 16 dimensions per transposing ldmatrix
         uint32_t vb[4];
         ldsm_x4_t(v_s + swz(r0 + (lane & 7) + ((lane >> 3) & 1) * 8, 2 * jj + (lane >> 4)), vb);
         mma_16816<true>(o[2 * jj], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
-        mma_16816<true>(o[2 * jj], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
         mma_16816<true>(o[2 * jj + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
-        mma_16816<true>(o[2 * jj + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
       }
     }
   }
@@ -368,51 +377,89 @@ __global__ void __launch_bounds__(kAttnThreads, 1) attention_kernel(const AttnPa
     l0 += __shfl_xor_sync(0xffffffffu, l0, off);
     l1 += __shfl_xor_sync(0xffffffffu, l1, off);
   }
-  if (t == 0) {
-    wm[warp * 16 + g] = m0;
-    wm[warp * 16 + g + 8] = m1;
-    wl[warp * 16 + g] = l0;
-    wl[warp * 16 + g + 8] = l1;
-  }
-  __syncthreads();  // every warp is past its last tile: kbuf/vbuf become ob
-  float M0 = -INFINITY, M1 = -INFINITY;
-  for (int w = 0; w < kAttnWarps; ++w) {
-    M0 = fmaxf(M0, wm[w * 16 + g]);
-    M1 = fmaxf(M1, wm[w * 16 + g + 8]);
-  }
-  if (tid < 16) {
-    float M = -INFINITY, L = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * 16 + tid]);
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float mw = wm[w * 16 + tid];
-      if (mw != -INFINITY) L = fmaf(wl[w * 16 + tid], exp2f(mw - M), L);
+  if (W == 1) {  // warp 0 holds every position of this CTA: no cross-warp merge
+    if (S == 1) {
+      if (warp == 0) {
+        // rows < G saw at least one position, so l >= 1
+        const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+        uint16_t* out = p.out + (size_t)kvh * G * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (g < G)
+            *reinterpret_cast<uint32_t*>(out + g * kHeadDim + 8 * j + 2 * t) =
+                pack_bf16x2(o[j][0] * i0, o[j][1] * i0);
+          if (g + 8 < G)
+            *reinterpret_cast<uint32_t*>(out + (g + 8) * kHeadDim + 8 * j + 2 * t) =
+                pack_bf16x2(o[j][2] * i1, o[j][3] * i1);
+        }
+      }
+      return;
     }
-    rm[tid] = M;
-    rl[tid] = L;
-  }
-  const float f0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
-  const float f1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+    if (warp == 0) {  // this CTA's partial for the cluster merge
+      if (t == 0) {
+        rm[g] = m0;
+        rm[g + 8] = m1;
+        rl[g] = l0;
+        rl[g + 8] = l1;
+      }
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    if (g < G)
-      *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g) * kObPitch + 8 * j + 2 * t) =
-          make_float2(o[j][0] * f0, o[j][1] * f0);
-    if (g + 8 < G)
-      *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g + 8) * kObPitch + 8 * j + 2 * t) =
-          make_float2(o[j][2] * f1, o[j][3] * f1);
+      for (int j = 0; j < 16; ++j) {
+        if (g < G)
+          *reinterpret_cast<float2*>(cpart + g * kHeadDim + 8 * j + 2 * t) =
+              make_float2(o[j][0], o[j][1]);
+        if (g + 8 < G)
+          *reinterpret_cast<float2*>(cpart + (g + 8) * kHeadDim + 8 * j + 2 * t) =
+              make_float2(o[j][2], o[j][3]);
+      }
+    }
+  } else {
+    if (t == 0) {
+      wm[warp * 16 + g] = m0;
+      wm[warp * 16 + g + 8] = m1;
+      wl[warp * 16 + g] = l0;
+      wl[warp * 16 + g + 8] = l1;
+    }
+    __syncthreads();  // every warp is past its last tile: kbuf/vbuf become ob
+    float M0 = -INFINITY, M1 = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      M0 = fmaxf(M0, wm[w * 16 + g]);
+      M1 = fmaxf(M1, wm[w * 16 + g + 8]);
+    }
+    if (tid < 16) {
+      float M = -INFINITY, L = 0.f;
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * 16 + tid]);
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float mw = wm[w * 16 + tid];
+        if (mw != -INFINITY) L = fmaf(wl[w * 16 + tid], exp2f(mw - M), L);
+      }
+      rm[tid] = M;
+      rl[tid] = L;
+    }
+    const float f0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+    const float f1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+    if (warp < W) {
+  #pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (g < G)
+          *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g) * kObPitch + 8 * j + 2 * t) =
+              make_float2(o[j][0] * f0, o[j][1] * f0);
+        if (g + 8 < G)
+          *reinterpret_cast<float2*>(ob + ((size_t)warp * G + g + 8) * kObPitch + 8 * j + 2 * t) =
+              make_float2(o[j][2] * f1, o[j][3] * f1);
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < G * kHeadDim; e += kAttnThreads) {
+      const int h = e >> 7, d = e & (kHeadDim - 1);
+      float acc = 0.f;
+      for (int w = 0; w < W; ++w) acc += ob[((size_t)w * G + h) * kObPitch + d];
+      if (S == 1)
+        p.out[(size_t)(kvh * G + h) * kHeadDim + d] = to_bf(acc / rl[h]);
+      else
+        cpart[e] = acc;
+    }
+    if (S == 1) return;
   }
-  __syncthreads();
-  for (int e = tid; e < G * kHeadDim; e += kAttnThreads) {
-    const int h = e >> 7, d = e & (kHeadDim - 1);
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) acc += ob[((size_t)w * G + h) * kObPitch + d];
-    if (S == 1)
-      p.out[(size_t)(kvh * G + h) * kHeadDim + d] = to_bf(acc / rl[h]);
-    else
-      cpart[e] = acc;
-  }
-  if (S == 1) return;
 
   // ---- merge the CTAs of this KV head over DSMEM (rank order); an idle CTA
   // (rank >= S) contributes m = -inf, l = 0

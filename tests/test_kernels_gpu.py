@@ -476,3 +476,60 @@ def test_fused_swiglu_epilogue_matches_unfused(M):
     with pytest.raises(NotImplementedError):  # and runs without a K split
         K.fused_launch(x, p, s, act, _lib.GemvConfig(2, 4, 2, 2, 0), _lib.W4_PRO_RMSNORM, nw,
                        1e-6, _lib.W4_EPI_SWIGLU)
+
+
+@pytest.mark.parametrize("split", [1, 4, 8])
+@pytest.mark.parametrize("M", [1, 2, 9])
+def test_fused_residual_epilogue_is_round_of_plain_plus_residual(split, M):
+    """The residual epilogue (its own kernel instance for bf16 and M <= 8, the
+    generic one otherwise), with and without split K: y <- round(r + round(y))
+    equals the plain GEMV's rounded output added to r and rounded, bit for bit,
+    also when y aliases r."""
+    from roofline_decoding_b200 import _lib
+
+    Kd, N = 2048, 512
+    p, s = pack_dev(gen(Kd, N, seed=40 + split))
+    rng = np.random.default_rng(split * 10 + M)
+    x = _bf16_dev(rng.standard_normal((M, Kd)))
+    r = _bf16_dev(rng.standard_normal((M, N)))
+    cfg = _lib.GemvConfig(1, 8, 2, split, 0)
+    plain = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
+    K.fused_launch(x, p, s, plain, cfg)
+    y = r.clone()
+    K.fused_launch(x, p, s, y, cfg, epilogue=_lib.W4_EPI_RESIDUAL, epi_src=y)
+    want = (r.float() + plain.float()).to(torch.bfloat16)
+    assert torch.equal(y, want)
+
+
+@pytest.mark.parametrize("pro,epi", [(1, 0), (1, 1), (2, 1), (0, 1), (2, 0)])
+@pytest.mark.parametrize("xdt", ["bf16", "fp16"])
+def test_every_prologue_epilogue_pair(pro, epi, xdt):
+    """Every (prologue, epilogue) pair, whichever kernel instance serves it,
+    against a host restatement: the prologue applied to x in float64 with the
+    kernel's bf16/fp16 roundings, then x @ dequant(W) + epilogue."""
+    from roofline_decoding_b200 import _lib
+
+    Kd, N, M = 1024, 256, 2
+    tdt = torch.bfloat16 if xdt == "bf16" else torch.float16
+    p, s, w_ex = _fused_case(Kd, N, M, 50 + pro * 3 + epi)
+    rng = np.random.default_rng(pro * 7 + epi)
+    xin = torch.from_numpy(rng.standard_normal((M, 2 * Kd if pro == 2 else Kd))).to(tdt).to(DEV)
+    nw = torch.from_numpy(1.0 + 0.05 * rng.standard_normal(Kd)).to(tdt).to(DEV)
+    b = torch.from_numpy(0.1 * rng.standard_normal(N)).to(tdt).to(DEV)
+    y = torch.empty((M, N), dtype=tdt, device=DEV)
+    cfg = K.default_config(M, Kd, N)
+    K.fused_launch(xin, p, s, y, cfg, pro, nw if pro == 1 else None, 1e-6, epi,
+                   b if epi == 1 else None)
+    xf = xin.float()
+    if pro == 1:
+        xn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(tdt)
+        xs = (nw * xn).float()
+    elif pro == 2:
+        g, u = xf[:, :Kd], xf[:, Kd:]
+        xs = ((g / (1.0 + torch.exp(-g))).to(tdt) * u.to(tdt)).float()
+    else:
+        xs = xf
+    want = xs.double() @ w_ex
+    if epi == 1:
+        want = want + b.double()
+    torch.testing.assert_close(y.double(), want, rtol=2 ** -7, atol=2e-2)
