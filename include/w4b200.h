@@ -176,9 +176,10 @@ typedef struct {
   int epilogue;            /* W4_EPI_BIAS: y <- y + bias[n];
                               W4_EPI_RESIDUAL: y <- residual + round(y) (may alias y);
                               W4_EPI_SWIGLU: the columns hold gate and up in alternating
-                              blocks of 32 (gate 0..31, up 0..31, gate 32..63, ...), and
-                              y [M, N/2] <- round(round(silu(round(gate))) * round(up)).
-                              Needs strips = 2 and split = 1; epi_src unused */
+                              blocks of B = 16 * strips (gate 0..B-1, up 0..B-1, gate
+                              B..2B-1, ...), and y [M, N/2] <-
+                              round(round(silu(round(gate))) * round(up)). Needs split = 1
+                              and bf16 x with at most 8 rows; epi_src unused */
   const void* epi_src;     /* bias [N] or residual [M, N] (y's type) */
 } w4_fused_ops;
 

@@ -307,10 +307,11 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void*
   if (ops->epilogue < W4_EPI_NONE || ops->epilogue > W4_EPI_SWIGLU)
     return fail(W4_ERR_INVALID_ARG, "w4_gemv_fused: epilogue %d unknown", ops->epilogue);
   if (ops->epilogue == W4_EPI_SWIGLU &&
-      (cfg->strips != 2 || cfg->split != 1 || N % 64 != 0 || x_dtype != W4_BF16 || M > 8))
+      (cfg->split != 1 || cfg->strips < 1 || N % (32 * cfg->strips) != 0 || x_dtype != W4_BF16 ||
+       M > 8))
     return fail(W4_ERR_UNSUPPORTED,
-                "w4_gemv_fused: the SwiGLU epilogue needs strips = 2, split = 1, N %% 64 == 0, "
-                "bf16 x and at most 8 rows");
+                "w4_gemv_fused: the SwiGLU epilogue needs split = 1, N a multiple of the tile "
+                "(32 * strips), bf16 x and at most 8 rows");
   if (ops->prologue == W4_PRO_RMSNORM && (!ops->norm_weight || !aligned16(ops->norm_weight)))
     return fail(W4_ERR_ALIGNMENT, "w4_gemv_fused: RMSNorm weight missing or not 16-byte aligned");
   if (ops->prologue != W4_PRO_NONE && x_dtype != y_dtype)

@@ -13,8 +13,7 @@ void* gemv_kernel_fused(int ops, int sw, int rg) {
     case kOpsRms: return gemv_pick_tile<true, 1, kOpsRms>(sw, rg);
     case kOpsResidual: return gemv_pick_tile<true, 1, kOpsResidual>(sw, rg);
     case kOpsSwigluResidual: return gemv_pick_tile<true, 1, kOpsSwigluResidual>(sw, rg);
-    // the SwiGLU epilogue pairs a gate strip with an up strip: two strips only
-    case kOpsRmsSwiglu: return sw == 2 ? gemv_pick_tile<true, 1, kOpsRmsSwiglu>(sw, rg) : nullptr;
+    case kOpsRmsSwiglu: return gemv_pick_tile<true, 1, kOpsRmsSwiglu>(sw, rg);
     default: return nullptr;
   }
 }

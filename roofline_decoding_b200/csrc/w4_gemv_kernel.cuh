@@ -721,10 +721,11 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
 
   // Row groups -> plane 0, in a fixed order.
   if (epi == W4_EPI_SWIGLU) {
-    // Two strips: gate columns then the matching up columns (the weights
-    // alternate blocks of 32); y has half the columns. The bf16 arithmetic of
-    // the reference model's MLP: gate and up rounded, silu in fp32 rounded,
-    // the product rounded by the store. Host-checked: SW == 2, no split.
+    // The tile's first half holds gate columns, its second half the matching
+    // up columns (the weights alternate blocks of half a tile, 16 * SW); y
+    // has half the columns. The bf16 arithmetic of the reference model's MLP:
+    // gate and up rounded, silu in fp32 rounded, the product rounded by the
+    // store. Host-checked: no split.
     constexpr int kHalf = T::kNT / 2;
     for (int o = threadIdx.x; o < M * kHalf; o += T::kThreads) {
       const int m = o / kHalf, c = o - m * kHalf;

@@ -81,7 +81,10 @@ class W4DecodeModel:
     """Static-KV, graph-captured batch-1 greedy decoder with int4 linears."""
 
     MODES = ("mega", "fused", "torch")
-    GU_BLOCK = 32  # gate/up interleave of the fused step (the GEMV strip width)
+    # The fused step's gate|up GEMV tile: the SwiGLU epilogue pairs the first and
+    # second half of a tile, so gate and up alternate in blocks of half a tile.
+    GU_CONFIG = (2, 4, 2, 1, 0)
+    GU_BLOCK = 16 * GU_CONFIG[0]
 
     @staticmethod
     def interleave_gate_up(w: torch.Tensor, block: int) -> torch.Tensor:
@@ -272,8 +275,8 @@ class W4DecodeModel:
             out = {}
             for name, (K, N) in shapes.items():
                 c = tuned_config(1, K, N, bf, bf, None, None, self.device)
-                if name == "gu" and self.gu_block and (c.strips != 2 or c.split != 1):
-                    c = GemvConfig(2, 4, 2, 1, 0)  # the SwiGLU epilogue pairs two strips
+                if name == "gu" and self.gu_block:
+                    c = GemvConfig(*self.GU_CONFIG)  # the tile the columns are interleaved for
                 out[name] = c.with_pdl(1 if self.pdl else 0)
             self._cfgs = out
         return self._cfgs

@@ -359,8 +359,8 @@ def fused_launch(x2: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
     _lib.W4_PRO_SWIGLU (x is [M, 2K] gate|up, x <- silu(gate) * up);
     epilogue: _lib.W4_EPI_BIAS (y += epi_src[n]), _lib.W4_EPI_RESIDUAL
     (y <- epi_src + round(y); epi_src may be y itself) or _lib.W4_EPI_SWIGLU (the
-    weight columns alternate gate and up in blocks of 32; y [M, N/2] <-
-    silu(gate) * up; needs a two-strip tile without split).
+    weight columns alternate gate and up in blocks of 16 * cfg.strips; y [M, N/2]
+    <- silu(gate) * up; needs a tile without split).
     """
     M = x2.shape[0]
     K = packed.shape[0] * 8

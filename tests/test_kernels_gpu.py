@@ -443,38 +443,37 @@ def test_fused_ops_reject_bad_arguments():
 
 
 @pytest.mark.parametrize("M", [1, 3])
-def test_fused_swiglu_epilogue_matches_unfused(M):
+@pytest.mark.parametrize("strips,row_groups", [(1, 8), (2, 4), (4, 2)])
+def test_fused_swiglu_epilogue_matches_unfused(M, strips, row_groups):
     """RMSNorm prologue + SwiGLU epilogue on gate/up columns interleaved in blocks
-    of 32 equals, bit for bit, the same GEMV without the epilogue followed by
-    round(round(silu(gate)) * up) on its bf16 outputs (the down projection's
-    SwiGLU prologue arithmetic)."""
+    of half a tile (16 * strips) against the same GEMV without the epilogue
+    followed by round(round(silu(gate)) * up) on its bf16 outputs (the down
+    projection's SwiGLU prologue arithmetic)."""
     from roofline_decoding_b200 import _lib
     from roofline_decoding_b200.decode import W4DecodeModel
 
     Kd, inter = 1536, 512
     rng = np.random.default_rng(7)
     w = torch.from_numpy((rng.standard_normal((Kd, 2 * inter)) * 0.02).astype(np.float16))
-    w_int = W4DecodeModel.interleave_gate_up(w, 32)
+    block = 16 * strips
+    w_int = W4DecodeModel.interleave_gate_up(w, block)
     p, s = K.pack_weights(w_int.to(DEV))
     x = _bf16_dev(rng.standard_normal((M, Kd)))
     nw = _bf16_dev(1.0 + 0.05 * rng.standard_normal(Kd))
-    cfg = _lib.GemvConfig(2, 4, 2, 1, 0)
+    cfg = _lib.GemvConfig(strips, row_groups, 2, 1, 0)
     act = torch.empty((M, inter), dtype=torch.bfloat16, device=DEV)
     full = torch.empty((M, 2 * inter), dtype=torch.bfloat16, device=DEV)
     K.fused_launch(x, p, s, act, cfg, _lib.W4_PRO_RMSNORM, nw, 1e-6, _lib.W4_EPI_SWIGLU)
     K.fused_launch(x, p, s, full, cfg, _lib.W4_PRO_RMSNORM, nw, 1e-6)
-    gu = W4DecodeModel.deinterleave_gate_up(full, 32).float()
+    gu = W4DecodeModel.deinterleave_gate_up(full, block).float()
     g, u = gu[:, :inter], gu[:, inter:]
     sg = (g / (1.0 + torch.exp(-g))).to(torch.bfloat16).float()
     want = (sg * u).to(torch.bfloat16)
     # __expf vs torch.exp can differ in the last bits of silu before its bf16 rounding
     torch.testing.assert_close(act.float(), want.float(), rtol=2 ** -7, atol=1e-3)
     assert (act == want).float().mean().item() > 0.99
-    with pytest.raises(NotImplementedError):  # the epilogue pairs exactly two strips
-        K.fused_launch(x, p, s, act, _lib.GemvConfig(1, 8, 2, 1, 0), _lib.W4_PRO_RMSNORM, nw,
-                       1e-6, _lib.W4_EPI_SWIGLU)
-    with pytest.raises(NotImplementedError):  # and runs without a K split
-        K.fused_launch(x, p, s, act, _lib.GemvConfig(2, 4, 2, 2, 0), _lib.W4_PRO_RMSNORM, nw,
+    with pytest.raises(NotImplementedError):  # the epilogue runs without a K split
+        K.fused_launch(x, p, s, act, _lib.GemvConfig(strips, row_groups, 2, 2, 0), _lib.W4_PRO_RMSNORM, nw,
                        1e-6, _lib.W4_EPI_SWIGLU)
 
 
