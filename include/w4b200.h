@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define W4B200_VERSION 100 /* 1.0.0 */
+#define W4B200_VERSION 110 /* 1.1.0 */
 #define W4B200_GROUP_SIZE 128
 #define W4B200_MAX_M 16
 
@@ -50,6 +50,13 @@ typedef struct {
   int stages;     /* shared-memory pipeline depth, 2..8                      */
   int split;      /* CTAs per cluster along K (deterministic DSMEM reduce)   */
   int pdl;        /* 1: launch with programmatic dependent launch            */
+  int columns;    /* CTA columns along N: 0 = one CTA per column tile; C less
+                   * than the tile count T gives CTA column i the tiles
+                   * i, i + C, i + 2C, ..., streamed back to back (a GPU-
+                   * filling grid for large N; 16 compute warps, strips x
+                   * row_groups = 2 x 8 or 4 x 4, exist in this mode only).
+                   * C < T needs no epilogue and a local output
+                   * (W4_ERR_UNSUPPORTED otherwise).                         */
 } w4_gemv_config;
 
 /* Library version (W4B200_VERSION). */

@@ -28,17 +28,19 @@ class W4Error(RuntimeError):
 
 class GemvConfig(ctypes.Structure):
     """w4_gemv_config (include/w4b200.h), as a tuple (strips, row_groups,
-    stages, split, pdl)."""
+    stages, split, pdl, columns); a 5-tuple leaves columns 0."""
     _fields_ = [
         ("strips", ctypes.c_int),
         ("row_groups", ctypes.c_int),
         ("stages", ctypes.c_int),
         ("split", ctypes.c_int),
         ("pdl", ctypes.c_int),
+        ("columns", ctypes.c_int),
     ]
 
-    def as_tuple(self) -> tuple[int, int, int, int, int]:
-        return (self.strips, self.row_groups, self.stages, self.split, self.pdl)
+    def as_tuple(self) -> tuple[int, ...]:
+        t = (self.strips, self.row_groups, self.stages, self.split, self.pdl)
+        return t + (self.columns,) if self.columns else t
 
     @classmethod
     def from_tuple(cls, t) -> "GemvConfig":
@@ -51,8 +53,8 @@ class GemvConfig(ctypes.Structure):
         return c
 
     def __repr__(self) -> str:
-        return ("GemvConfig(strips=%d, row_groups=%d, stages=%d, split=%d, pdl=%d)"
-                % self.as_tuple())
+        return ("GemvConfig(strips=%d, row_groups=%d, stages=%d, split=%d, pdl=%d, columns=%d)"
+                % (self.as_tuple() + (0,))[:6])
 
 
 W4_PRO_NONE, W4_PRO_RMSNORM, W4_PRO_SWIGLU = 0, 1, 2

@@ -17,10 +17,13 @@ void* gemv_kernel_plain(int bf16, int mb, int sw, int rg) {
 
 namespace {
 
-// The instance a launch uses: plain, the fused decode combination it matches
-// (bf16 activations, up to 8 batch rows), or the generic one.
-void* pick_kernel(int bf16, int mb, int sw, int rg, int ops) {
-  if (ops == kOpsPlain) return gemv_kernel_plain(bf16, mb, sw, rg);
+// The instance a launch uses: plain (one or several tiles per CTA column),
+// the fused decode combination it matches (bf16 activations, up to 8 batch
+// rows), or the generic one.
+void* pick_kernel(int bf16, int mb, int sw, int rg, int ops, bool tiles) {
+  if (ops == kOpsPlain)
+    return tiles ? gemv_kernel_plain_tiles(bf16, mb, sw, rg) : gemv_kernel_plain(bf16, mb, sw, rg);
+  if (tiles) return gemv_kernel_generic(bf16, mb, sw, rg);
   if (ops >= kOpsFusedFirst && ops <= kOpsFusedLast && bf16 && mb == 1)
     return gemv_kernel_fused(ops, sw, rg);
   return gemv_kernel_generic(bf16, mb, sw, rg);
@@ -30,31 +33,51 @@ constexpr int kSW[] = {1, 2, 4};
 
 }  // namespace
 
-size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& c) {
+int gemv_tiles(int N, const w4_gemv_config& c) {
+  const int nt = 32 * c.strips;
+  return (N + nt - 1) / nt;
+}
+
+int gemv_columns(int N, const w4_gemv_config& c) {
+  const int t = gemv_tiles(N, c);
+  return (c.columns > 0 && c.columns < t) ? c.columns : t;
+}
+
+size_t gemv_smem_bytes(int M, int K, int N, const w4_gemv_config& c) {
   const int groups = K / 128;
+  const int cols = gemv_columns(N, c);
+  const size_t tiles_per_cta = (gemv_tiles(N, c) + cols - 1) / cols;
   const int gps = (groups + c.split - 1) / c.split;
   const size_t nt = 32 * (size_t)c.strips;
   const size_t stage = (size_t)c.strips * c.row_groups * 16 * 128;
   const size_t scale = ((size_t)c.row_groups * nt * 2 + 127) / 128 * 128;
   const size_t plane = (size_t)gps * 16 * 16 + 16;
-  const size_t beta = (((size_t)M * gps + 3) & ~(size_t)3) * 4 + 16 * 4;
+  // beta and 2^-e per (row, group), then 1/rms per row
+  const size_t beta = (((size_t)M * gps + 3) & ~(size_t)3) * 4 * 2 + 16 * 4;
   const size_t tile = (size_t)M * nt * 4;
-  return 1024 + c.stages * (stage + scale) + M * plane + beta + c.row_groups * tile +
-         tile /* epilogue operands */ + 2 * c.stages * sizeof(uint64_t) + 16;  // + the epoch word
+  return 1024 + c.stages * (stage + scale) + M * plane + beta +
+         tiles_per_cta * c.row_groups * tile + tile /* epilogue operands */ + 2 * c.stages * sizeof(uint64_t) + 16;  // + the epoch word
 }
 
 int gemv_validate_config(int M, int K, int N, const w4_gemv_config& c, const DeviceInfo& di) {
-  (void)N;
-  if (!gemv_kernel_plain(0, 1, c.strips, c.row_groups))
+  if (c.strips < 1 || c.row_groups < 1)
     return fail(W4_ERR_INVALID_ARG, "unsupported tile strips=%d row_groups=%d", c.strips,
                 c.row_groups);
+  const bool several = gemv_columns(N, c) < gemv_tiles(N, c);
+  if (!gemv_kernel_plain(0, 1, c.strips, c.row_groups) &&
+      !(several && gemv_kernel_plain_tiles(0, 1, c.strips, c.row_groups)))
+    return fail(W4_ERR_INVALID_ARG,
+                "unsupported tile strips=%d row_groups=%d (16 compute warps need fewer CTA "
+                "columns than tiles)",
+                c.strips, c.row_groups);
   if (c.stages < 2 || c.stages > 8)
     return fail(W4_ERR_INVALID_ARG, "stages=%d outside 2..8", c.stages);
   if (c.split < 1 || c.split > 16)
     return fail(W4_ERR_INVALID_ARG, "split=%d outside 1..16", c.split);
   if (c.split > K / 128)
     return fail(W4_ERR_INVALID_ARG, "split=%d exceeds the %d K groups", c.split, K / 128);
-  const size_t smem = gemv_smem_bytes(M, K, c);
+  if (c.columns < 0) return fail(W4_ERR_INVALID_ARG, "columns=%d is negative", c.columns);
+  const size_t smem = gemv_smem_bytes(M, K, N, c);
   if (smem > (size_t)di.max_smem_optin)
     return fail(W4_ERR_UNSUPPORTED,
                 "tile needs %zu B of shared memory (device allows %d); raise split", smem,
@@ -96,9 +119,9 @@ int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const De
   // Keep the whole share in flight when it is small (each stage that waits
   // for a free slot costs a DRAM round trip); 6 slots suffice for streaming.
   c.stages = std::max(2, std::min(6, stages_needed));
-  while (c.stages > 2 && gemv_smem_bytes(M, K, c) > (size_t)di.max_smem_optin / 2) --c.stages;
+  while (c.stages > 2 && gemv_smem_bytes(M, K, N, c) > (size_t)di.max_smem_optin / 2) --c.stages;
   // Grow the split until the activation slice fits in shared memory.
-  while (gemv_smem_bytes(M, K, c) > (size_t)di.max_smem_optin && c.split < 16 &&
+  while (gemv_smem_bytes(M, K, N, c) > (size_t)di.max_smem_optin && c.split < 16 &&
          c.split < groups && split_k <= 0)
     ++c.split;
   *out = c;
@@ -160,10 +183,12 @@ static int gemv_kernel_attributes(void* k, const DeviceInfo& di);
 int gemv_init_device(const DeviceInfo& di) {
   for (int sw : kSW)
     for (int rg = 1; rg <= 8; rg *= 2) {
-      if (!gemv_kernel_plain(0, 1, sw, rg)) continue;
+      if (!gemv_kernel_plain_tiles(0, 1, sw, rg)) continue;
       for (int b = 0; b < 2; ++b)
         for (int mb = 1; mb <= 2; ++mb)
-          for (void* k : {gemv_kernel_plain(b, mb, sw, rg), gemv_kernel_generic(b, mb, sw, rg)}) {
+          for (void* k : {gemv_kernel_plain(b, mb, sw, rg), gemv_kernel_generic(b, mb, sw, rg),
+                          gemv_kernel_plain_tiles(b, mb, sw, rg)}) {
+            if (!k) continue;  // the 16-warp tiles exist as plain-tiles instances only
             const int st = gemv_kernel_attributes(k, di);
             if (st != W4_OK) return st;
           }
@@ -214,10 +239,19 @@ static int gemv_prepare(const GemvLaunch& L, GemvPrepared* g) {
   const w4_gemv_config& c = L.cfg;
   st = gemv_validate_config(L.M, L.K, L.N, c, di);
   if (st != W4_OK) return st;
+  const int tiles = gemv_tiles(L.N, c);
+  const int columns = gemv_columns(L.N, c);
+  if (columns < tiles && (L.ops.epilogue != W4_EPI_NONE || L.peer))
+    return fail(W4_ERR_UNSUPPORTED,
+                "columns=%d below the %d column tiles needs no epilogue and a local output",
+                columns, tiles);
 
   const int mb = L.M > 8 ? 2 : 1;
   const int ops = L.peer ? kOpsGeneric : ops_for(L.ops.prologue, L.ops.epilogue);
-  g->kfn = pick_kernel(L.x_bf16, mb, c.strips, c.row_groups, ops);
+  g->kfn = pick_kernel(L.x_bf16, mb, c.strips, c.row_groups, ops, columns < tiles);
+  if (!g->kfn)
+    return fail(W4_ERR_UNSUPPORTED, "tile strips=%d row_groups=%d has no instance with a prologue",
+                c.strips, c.row_groups);
   const int nt = 32 * c.strips;
   const int rows = L.K / 8;
 
@@ -238,6 +272,8 @@ static int gemv_prepare(const GemvLaunch& L, GemvPrepared* g) {
   p.N = L.N;
   p.groups_total = L.K / 128;
   p.groups_per_split = (p.groups_total + c.split - 1) / c.split;
+  p.n_tiles = tiles;
+  p.tiles_per_cta = (tiles + columns - 1) / columns;
   p.stages = c.stages;
   p.y_bf16 = L.y_bf16;
   p.err = di.err_word;
@@ -247,9 +283,9 @@ static int gemv_prepare(const GemvLaunch& L, GemvPrepared* g) {
   p.epi = L.ops.epilogue;
   p.epi_src = L.ops.epi_src;
 
-  g->grid = dim3((unsigned)((L.N + nt - 1) / nt), (unsigned)c.split, 1);
+  g->grid = dim3((unsigned)columns, (unsigned)c.split, 1);
   g->block = dim3((unsigned)((c.strips * c.row_groups + 1) * 32), 1, 1);
-  g->smem = gemv_smem_bytes(L.M, L.K, c);
+  g->smem = gemv_smem_bytes(L.M, L.K, L.N, c);
   int na = 0;
   if (c.split > 1) {
     g->attrs[na].id = cudaLaunchAttributeClusterDimension;

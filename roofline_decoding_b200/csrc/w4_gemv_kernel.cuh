@@ -7,7 +7,14 @@
 // and :163-208 (_fused_gemv_v3_kernel), on the reference's packed layout.
 //
 // Work decomposition
-//   CTA tile    : 32*SW output columns x one K slice (a "split").
+//   CTA tile    : 32*SW output columns x one K slice (a "split"). With fewer
+//                 CTA columns C than tiles T (large N), CTA column i takes
+//                 the tiles i, i + C, i + 2C, ... and its producer streams
+//                 them back to back through one ring; the x slice is staged
+//                 once, and each tile's partial sums stay in shared memory
+//                 until the common epilogue. These streaming instances also
+//                 come with 16 compute warps (one CTA per SM) and stage bf16
+//                 activations as fp16 (a cheaper unpack in the K loop).
 //   Warps       : SW*RG compute warps + 1 producer warp. Compute warp w owns
 //                 strip w % SW (32 columns) and row group w / SW.
 //   Stage       : RG K-groups (RG * 16 packed rows) for all SW strips, i.e.
@@ -52,6 +59,8 @@ struct GemvParams {
   int M, K, N;
   int groups_total;      // K / 128
   int groups_per_split;  // K groups handled by one CTA
+  int n_tiles;           // column tiles (32*SW columns each) covering N
+  int tiles_per_cta;     // most tiles one CTA column takes (partial-sum space)
   int stages;            // ring depth
   int y_bf16;
   int* err;  // device error word
@@ -96,8 +105,12 @@ enum : int {
   kOpsResidual = 4,        // residual epilogue (o)
   kOpsSwigluResidual = 5,  // SwiGLU prologue, residual epilogue (down)
   kOpsRmsSwiglu = 6,       // RMSNorm prologue, SwiGLU epilogue (gate|up, interleaved)
+  kOpsPlainTiles = 7,      // plain, CTA columns streaming several column tiles
 };
 constexpr int kOpsFusedFirst = kOpsRmsBias, kOpsFusedLast = kOpsRmsSwiglu;
+// Instances whose CTA columns may take several column tiles (the others are
+// compiled for one tile per CTA: the loop over tiles costs registers).
+constexpr bool ops_tiles(int ops) { return ops == kOpsGeneric || ops == kOpsPlainTiles; }
 constexpr int ops_pro(int ops) {
   return (ops == kOpsRmsBias || ops == kOpsRms || ops == kOpsRmsSwiglu) ? W4_PRO_RMSNORM
          : ops == kOpsSwigluResidual            ? W4_PRO_SWIGLU
@@ -192,22 +205,53 @@ __device__ __forceinline__ void report_error(int* err, int code) {
 }
 
 // Reorders the 8 activations of one packed row into the order the MMA
-// fragments consume them: (x0,x4) (x1,x5) (x2,x6) (x3,x7). For fp16 the odd
+// fragments consume them: (x0,x4) (x1,x5) (x2,x6) (x3,x7). In fp16 the odd
 // pairs meet the "1024 + 16q" form of unpack_nibbles and are pre-scaled by
 // 1/16 (exact for normal values; below 2^-10 the rounding error is under
 // 2^-25 absolute).
-template <bool kBF16>
+template <bool kBF16Math>
 __device__ __forceinline__ uint4 permute_row(uint4 v) {
   uint4 o;
   o.x = __byte_perm(v.x, v.z, 0x5410);
   o.y = __byte_perm(v.x, v.z, 0x7632);
   o.z = __byte_perm(v.y, v.w, 0x5410);
   o.w = __byte_perm(v.y, v.w, 0x7632);
-  if constexpr (!kBF16) {
+  if constexpr (!kBF16Math) {
     constexpr uint32_t kSixteenth = 0x2C002C00u;  // 1/16 | 1/16
     constexpr uint32_t kZero = 0x80008000u;       // -0 | -0 (keeps x * 1/16 exact)
     o.y = fma_f16x2(o.y, kSixteenth, kZero);
     o.w = fma_f16x2(o.w, kSixteenth, kZero);
+  }
+  return o;
+}
+
+// 8 bf16 activations of one packed row -> fp16, times the power of two 2^e
+// of their K group: 16 consecutive lanes hold the 16 rows of a group (every
+// lane of the warp calls this; lanes past the data pass zeros). The lane
+// with `leader` set stores the group's 2^-e to *pow_out.
+__device__ __forceinline__ uint4 bf16_row_to_f16(uint4 v, bool leader, float* pow_out) {
+  const uint32_t* vi = reinterpret_cast<const uint32_t*>(&v);
+  float f[8];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(vi[i] << 16);
+    f[2 * i + 1] = __uint_as_float(vi[i] & 0xFFFF0000u);
+    mx = fmaxf(mx, fmaxf(fabsf(f[2 * i]), fabsf(f[2 * i + 1])));
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  // biased exponent eb of mx: mx * 2^(141 - eb) lies in [2^14, 2^15)
+  const int eb = (int)((__float_as_uint(mx) >> 23) & 0xFFu);
+  const int e = mx > 0.f ? min(126, max(-126, 141 - eb)) : 0;
+  const float up = __uint_as_float((uint32_t)(127 + e) << 23);
+  if (leader) *pow_out = __uint_as_float((uint32_t)(127 - e) << 23);
+  uint4 o;
+  uint32_t* oi = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __floats2half2_rn(f[2 * i] * up, f[2 * i + 1] * up);
+    oi[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
   return o;
 }
@@ -240,11 +284,12 @@ __device__ __forceinline__ uint4 preload_norm_weight(const GemvParams& p, int g0
   return make_uint4(0u, 0u, 0u, 0u);
 }
 
-template <bool kBF16, int kCW>
+// kF16Math: bf16 rows are converted to fp16 for the MMAs (below).
+template <bool kBF16, int kCW, bool kF16Math>
 __device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, int g1, int gps,
                                                   uint8_t* s_x, int plane, float* s_beta,
-                                                  float* s_inv, float* s_red, int warp,
-                                                  int lane, uint4 pre, int pro) {
+                                                  float* s_pow, float* s_inv, float* s_red,
+                                                  int warp, int lane, uint4 pre, int pro) {
   constexpr int nct = kCW * 32;
   const int M = p.M;
   const int rows_slice = gps * 16;
@@ -345,23 +390,33 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, int g0, i
       if (b0 + u * nct >= total) break;  // uniform over the consumer threads
       const int idx = b0 + u * nct + threadIdx.x;
       float lo = 0.f, hi = 0.f;
-      uint4 o = make_uint4(0u, 0u, 0u, 0u);
+      int m = 0, r = 0;
       if (idx < total) {
-        const int m = idx / rows_slice;
-        const int r = idx - m * rows_slice;
-        const int krow = g0 * 16 + r;
-        if (pro != W4_PRO_NONE && krow < g1 * 16)
+        m = idx / rows_slice;
+        r = idx - m * rows_slice;
+        if (pro != W4_PRO_NONE && g0 * 16 + r < g1 * 16)
           v[u] = stage_transform<kBF16>(
               pro, v[u], aux[u],
               pro == W4_PRO_RMSNORM ? (rms_one_pass ? inv_one : s_inv[m]) : 0.f);
-        o = permute_row<kBF16>(v[u]);
+      }
+      // With kF16Math, bf16 rows enter the MMAs as fp16 (whose unpack costs 5
+      // operations per packed word against 7): every group is scaled by the
+      // power of two 2^e that puts its largest |x| in [2^14, 2^15), so the
+      // conversion is exact (8 significant bits into 11) for every element
+      // within 2^-28 of the group's largest; the group's sum is scaled back
+      // by 2^-e, also exact.
+      constexpr bool kBF16Math = kBF16 && !kF16Math;
+      if constexpr (kBF16 && kF16Math)
+        v[u] = bf16_row_to_f16(v[u], idx < total && (idx & 15) == 0, s_pow + (idx >> 4));
+      if (idx < total) {
+        const uint4 o = permute_row<kBF16Math>(v[u]);
         *reinterpret_cast<uint4*>(s_x + m * plane + r * 16) = o;
-        const float2 a = h2f2(o.x, kBF16), b = h2f2(o.y, kBF16);
-        const float2 c = h2f2(o.z, kBF16), d = h2f2(o.w, kBF16);
+        const float2 a = h2f2(o.x, kBF16Math), b = h2f2(o.y, kBF16Math);
+        const float2 c = h2f2(o.z, kBF16Math), d = h2f2(o.w, kBF16Math);
         lo = (a.x + a.y) + (c.x + c.y);
         hi = (b.x + b.y) + (d.x + d.y);
       }
-      float bsum = kBF16 ? kBF16Offset * (lo + hi) : kF16LowOffset * lo + kF16HighOffset * hi;
+      float bsum = kBF16Math ? kBF16Offset * (lo + hi) : kF16LowOffset * lo + kF16HighOffset * hi;
 #pragma unroll
       for (int off = 8; off > 0; off >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
       if (idx < total && (idx & 15) == 0) s_beta[idx >> 4] = bsum;
@@ -381,11 +436,13 @@ struct LaneView {
   uint32_t w_off[2];
   uint32_t x_off[MB];
   const float* b_row[MB][2];
+  int pow_off;  // s_pow - s_beta, in floats (bf16 activations: 2^-e per group)
   uint32_t sc_off;
 
   __device__ __forceinline__ LaneView(const uint8_t* s_w, const uint8_t* s_x, const uint8_t* s_sc,
-                                      const float* s_beta, int plane, int gps, int M, int strip,
-                                      int rg, int g, int t) {
+                                      const float* s_beta, int pow_off, int plane, int gps, int M,
+                                      int strip, int rg, int g, int t)
+      : pow_off(pow_off) {
     using T = TileShape<SW, RG>;
 #pragma unroll
     for (int e = 0; e < 2; ++e)
@@ -404,7 +461,9 @@ struct LaneView {
 // One K group of one stage for one compute warp: acc += s * sum_k (q - 8) x
 // over the group gl of the staged activations, its weights in the ring slot
 // at byte offset stage_base and its scales in the scale slot at sc.
-template <bool kBF16, int MB, int SW, int RG>
+// kBF16Math: bf16 MMAs on bf16 activations; otherwise fp16 MMAs, on fp16
+// activations or bf16 ones converted with a power of two per group (kPow).
+template <bool kBF16Math, bool kPow, int MB, int SW, int RG>
 __device__ __forceinline__ void mma_group(float (&acc)[2][MB][4], const LaneView<MB, SW, RG>& lv,
                                           uint32_t stage_base, uint32_t sc, int gl) {
   // accumulators start at -beta of their batch row: the MMA sums then
@@ -432,19 +491,19 @@ __device__ __forceinline__ void mma_group(float (&acc)[2][MB][4], const LaneView
 #pragma unroll
       for (int mb = 0; mb < MB; ++mb) xb[mb] = lds128(lv.x_off[mb] + xrow);
       uint32_t ha[4], hb[4];
-      unpack_nibbles<kBF16>(wv.x, ha);  // column 4g
-      unpack_nibbles<kBF16>(wv.y, hb);  // column 4g+1
+      unpack_nibbles<kBF16Math>(wv.x, ha);  // column 4g
+      unpack_nibbles<kBF16Math>(wv.y, hb);  // column 4g+1
 #pragma unroll
       for (int mb = 0; mb < MB; ++mb) {
-        mma_16816<kBF16>(c[0][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
-        mma_16816<kBF16>(c[0][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+        mma_16816<kBF16Math>(c[0][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+        mma_16816<kBF16Math>(c[0][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
       }
-      unpack_nibbles<kBF16>(wv.z, ha);  // column 4g+2
-      unpack_nibbles<kBF16>(wv.w, hb);  // column 4g+3
+      unpack_nibbles<kBF16Math>(wv.z, ha);  // column 4g+2
+      unpack_nibbles<kBF16Math>(wv.w, hb);  // column 4g+3
 #pragma unroll
       for (int mb = 0; mb < MB; ++mb) {
-        mma_16816<kBF16>(c[1][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
-        mma_16816<kBF16>(c[1][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
+        mma_16816<kBF16Math>(c[1][mb], ha[0], hb[0], ha[1], hb[1], xb[mb].x, xb[mb].y);
+        mma_16816<kBF16Math>(c[1][mb], ha[2], hb[2], ha[3], hb[3], xb[mb].z, xb[mb].w);
       }
     }
   }
@@ -455,14 +514,17 @@ __device__ __forceinline__ void mma_group(float (&acc)[2][MB][4], const LaneView
   const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&s23));
 #pragma unroll
   for (int mb = 0; mb < MB; ++mb) {
-    acc[0][mb][0] = fmaf(f01.x, c[0][mb][0], acc[0][mb][0]);
-    acc[0][mb][1] = fmaf(f01.x, c[0][mb][1], acc[0][mb][1]);
-    acc[0][mb][2] = fmaf(f01.y, c[0][mb][2], acc[0][mb][2]);
-    acc[0][mb][3] = fmaf(f01.y, c[0][mb][3], acc[0][mb][3]);
-    acc[1][mb][0] = fmaf(f23.x, c[1][mb][0], acc[1][mb][0]);
-    acc[1][mb][1] = fmaf(f23.x, c[1][mb][1], acc[1][mb][1]);
-    acc[1][mb][2] = fmaf(f23.y, c[1][mb][2], acc[1][mb][2]);
-    acc[1][mb][3] = fmaf(f23.y, c[1][mb][3], acc[1][mb][3]);
+    // bf16 activations: the group's 2^-e of batch rows 2t (i even), 2t+1 (i odd)
+    const float p0 = kPow ? lv.b_row[mb][0][gl + lv.pow_off] : 1.f;
+    const float p1 = kPow ? lv.b_row[mb][1][gl + lv.pow_off] : 1.f;
+    acc[0][mb][0] = fmaf(f01.x * p0, c[0][mb][0], acc[0][mb][0]);
+    acc[0][mb][1] = fmaf(f01.x * p1, c[0][mb][1], acc[0][mb][1]);
+    acc[0][mb][2] = fmaf(f01.y * p0, c[0][mb][2], acc[0][mb][2]);
+    acc[0][mb][3] = fmaf(f01.y * p1, c[0][mb][3], acc[0][mb][3]);
+    acc[1][mb][0] = fmaf(f23.x * p0, c[1][mb][0], acc[1][mb][0]);
+    acc[1][mb][1] = fmaf(f23.x * p1, c[1][mb][1], acc[1][mb][1]);
+    acc[1][mb][2] = fmaf(f23.y * p0, c[1][mb][2], acc[1][mb][2]);
+    acc[1][mb][3] = fmaf(f23.y * p1, c[1][mb][3], acc[1][mb][3]);
   }
 }
 
@@ -548,13 +610,15 @@ __device__ __forceinline__ void publish_gathered(const GemvParams& p, const Peer
 // projection's SwiGLU instance runs as a split-K grid of 2.6 CTAs per SM, so
 // it is held to three (72 registers): a grid that does not fit the SMs at
 // once runs in two waves.
-template <int OPS>
+// The 16-warp tiles (one CTA per SM, streaming) get the registers of one.
+template <int OPS, int THREADS>
 constexpr int gemv_min_blocks() {
-  return OPS == kOpsSwigluResidual ? 3 : 2;
+  return THREADS > 288 ? 1 : OPS == kOpsSwigluResidual ? 3 : 2;
 }
 
 template <bool kBF16, int MB, int SW, int RG, int OPS>
-__global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<OPS>())
+__global__ void __launch_bounds__(TileShape<SW, RG>::kThreads,
+                                  gemv_min_blocks<OPS, TileShape<SW, RG>::kThreads>())
     w4_gemv_kernel(const __grid_constant__ CUtensorMap tm_w,
                    const __grid_constant__ CUtensorMap tm_s, const GemvParams p,
                    const __grid_constant__ PeerParams pp) {
@@ -573,22 +637,36 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
   const int plane = gps * 16 * 16 + 16;  // +16 B: odd batch rows land on other banks
   const int tile_elems = M * T::kNT;
   const int nsplit = gridDim.y;
+  // this CTA column's tiles (one per CTA unless the grid has fewer columns)
+  constexpr bool kTiles = ops_tiles(OPS);
+  // bf16 activations: the streaming instances convert them to fp16 while
+  // staging (a cheaper unpack in the throughput-bound K loop); the others,
+  // run in chains of dependent launches, keep bf16 MMAs and the shorter
+  // staging path.
+  constexpr bool kF16Math = !kBF16 || OPS == kOpsPlainTiles;
+  // CTA column c takes the tiles c, c + C, c + 2C, ... (C = gridDim.x), so
+  // the CTAs running at once stream neighbouring columns (whole DRAM rows)
+  const int t_first = (int)blockIdx.x;
+  const int t_step = kTiles ? (int)gridDim.x : 1;
+  const int n_tl = kTiles ? (p.n_tiles - t_first + t_step - 1) / t_step : 1;
   uint8_t* s_w = smem;
   uint8_t* s_sc = s_w + S * T::kStageBytes;
   uint8_t* s_x = s_sc + S * T::kScaleSlot;
   // beta[m][group]: the constant the unpacked values carry, summed against the
   // staged activations of each group (subtracted through the accumulator init)
   float* s_beta = reinterpret_cast<float*>(s_x + M * plane);
-  float* s_inv = s_beta + ((M * gps + 3) & ~3);  // RMSNorm 1/rms per row
+  const int n_beta = (M * gps + 3) & ~3;
+  float* s_pow = s_beta + n_beta;  // bf16 activations: 2^-e per (row, group)
+  float* s_inv = s_pow + n_beta;   // RMSNorm 1/rms per row
   float* s_red = s_inv + 16;
-  float* s_epi = s_red + RG * tile_elems;  // epilogue operand per output element
+  float* s_epi = s_red + p.tiles_per_cta * RG * tile_elems;  // epilogue operand per element
   uint64_t* full = reinterpret_cast<uint64_t*>(s_epi + tile_elems);
   uint64_t* empty = full + S;
   unsigned& s_epoch = *reinterpret_cast<unsigned*>(empty + S);  // gathered output: this call's epoch
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * T::kNT;
+  const int n0 = t_first * T::kNT;  // first column (the single-tile epilogues use it)
   const int g0 = blockIdx.y * gps;
   const int g1 = min(p.groups_total, g0 + gps);
   const int n_groups = max(0, g1 - g0);
@@ -618,22 +696,27 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
       int issued = 0;
       int slot = 0;
       uint32_t phase = 0;  // phase of the current pass over the ring
-      for (int j = 0; j < n_stages; ++j) {
-        if (j >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
-          report_error(p.err, kErrEmptyWait);
-          break;
-        }
-        mbar_arrive_expect_tx(&full[slot], T::kStageBytes + T::kScaleBytes);
-        const int grp = g0 + j * RG;
+      bool ok = true;
+      for (int tl = 0; tl < n_tl && ok; ++tl) {
+        const int c0 = (t_first + tl * t_step) * T::kNT;
+        for (int j = 0; j < n_stages; ++j) {
+          if (issued >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
+            report_error(p.err, kErrEmptyWait);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[slot], T::kStageBytes + T::kScaleBytes);
+          const int grp = g0 + j * RG;
 #pragma unroll
-        for (int s = 0; s < SW; ++s)
-          tma_load_2d(s_w + slot * T::kStageBytes + s * T::kStripBytes, &tm_w, &full[slot],
-                      n0 + 32 * s, grp * 16);
-        tma_load_2d(s_sc + slot * T::kScaleSlot, &tm_s, &full[slot], n0, grp);
-        ++issued;
-        if (++slot == S) {
-          slot = 0;
-          phase ^= 1u;
+          for (int s = 0; s < SW; ++s)
+            tma_load_2d(s_w + slot * T::kStageBytes + s * T::kStripBytes, &tm_w, &full[slot],
+                        c0 + 32 * s, grp * 16);
+          tma_load_2d(s_sc + slot * T::kScaleSlot, &tm_s, &full[slot], c0, grp);
+          ++issued;
+          if (++slot == S) {
+            slot = 0;
+            phase ^= 1u;
+          }
         }
       }
       // Do not leave while copies into this CTA's shared memory are in flight.
@@ -671,8 +754,8 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
                      : 0.f;
       }
     }
-    stage_activations<kBF16, T::kCW>(p, g0, g1, gps, s_x, plane, s_beta, s_inv, s_red, warp,
-                                     lane, pre, pro);
+    stage_activations<kBF16, T::kCW, kF16Math>(p, g0, g1, gps, s_x, plane, s_beta, s_pow, s_inv, s_red,
+                                     warp, lane, pre, pro);
     if (residual) {
 #pragma unroll
       for (int r = 0; r < kResPerThread; ++r) {
@@ -685,37 +768,41 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
     const int rg = warp / SW;
     const int g = lane >> 2;
     const int t = lane & 3;
-    const LaneView<MB, SW, RG> lv(s_w, s_x, s_sc, s_beta, plane, gps, M, strip, rg, g, t);
-
-    // acc[tile][mb][i]: tile t covers columns 4g+2t (i = 0,1) and 4g+2t+1
-    // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
-    float acc[2][MB][4];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < MB; ++b)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
+    const LaneView<MB, SW, RG> lv(s_w, s_x, s_sc, s_beta, n_beta, plane, gps, M, strip, rg, g, t);
 
     int slot = 0;
     uint32_t phase = 0;
-    for (int j = 0; j < n_stages; ++j) {
-      if (!mbar_wait(&full[slot], phase)) {
-        report_error(p.err, kErrFullWait);
-        break;
+    bool ok = true;
+    for (int tl = 0; tl < n_tl && ok; ++tl) {
+      // acc[a][mb][i]: MMA tile a covers columns 4g+2a (i = 0,1) and 4g+2a+1
+      // (i = 2,3); i & 1 selects batch row 8*mb + 2*(lane&3) + (i&1).
+      float acc[2][MB][4];
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int b = 0; b < MB; ++b)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[a][b][i] = 0.f;
+
+      for (int j = 0; j < n_stages; ++j) {
+        if (!mbar_wait(&full[slot], phase)) {
+          report_error(p.err, kErrFullWait);
+          ok = false;
+          break;
+        }
+        const int gl = j * RG + rg;  // group inside the slice
+        if (gl < n_groups)
+          mma_group<kBF16 && !kF16Math, kBF16 && kF16Math, MB, SW, RG>(acc, lv, slot * T::kStageBytes,
+                                       lv.sc_off + slot * T::kScaleSlot, gl);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == S) {
+          slot = 0;
+          phase ^= 1u;
+        }
       }
-      const int gl = j * RG + rg;  // group inside the slice
-      if (gl < n_groups)
-        mma_group<kBF16, MB, SW, RG>(acc, lv, slot * T::kStageBytes,
-                                     lv.sc_off + slot * T::kScaleSlot, gl);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      if (++slot == S) {
-        slot = 0;
-        phase ^= 1u;
-      }
+      write_partials<MB, T::kNT>(acc, s_red + tl * RG * tile_elems, M, strip, rg, g, t);
     }
-    write_partials<MB, T::kNT>(acc, s_red, M, strip, rg, g, t);
   }
   __syncthreads();
 
@@ -748,33 +835,43 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads, gemv_min_blocks<O
     }
   } else if (nsplit == 1) {
     // each thread sums its elements' row groups and stores them itself
+    // (element i of the CTA's tiles: tile i / tile_elems, at i % tile_elems)
     const unsigned epoch = s_epoch;
-    for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {
-      float v = s_red[idx];
+    for (int idx = threadIdx.x; idx < n_tl * tile_elems; idx += T::kThreads) {
+      const int tl = kTiles ? idx / tile_elems : 0, e = idx - tl * tile_elems;
+      const float* r0 = s_red + tl * RG * tile_elems + e;
+      float v = r0[0];
 #pragma unroll
-      for (int r = 1; r < RG; ++r) v += s_red[r * tile_elems + idx];
-      store_out(p, pp, epi, world, epoch, idx / T::kNT, n0 + idx % T::kNT, v, s_epi[idx]);
+      for (int r = 1; r < RG; ++r) v += r0[r * tile_elems];
+      store_out(p, pp, epi, world, epoch, e / T::kNT, (t_first + tl * t_step) * T::kNT + e % T::kNT, v,
+                s_epi[e]);
     }
   } else {
     if (RG > 1) {
-      for (int idx = threadIdx.x; idx < tile_elems; idx += T::kThreads) {
-        float v = s_red[idx];
+      for (int idx = threadIdx.x; idx < n_tl * tile_elems; idx += T::kThreads) {
+        const int tl = kTiles ? idx / tile_elems : 0, e = idx - tl * tile_elems;
+        float* r0 = s_red + tl * RG * tile_elems + e;
+        float v = r0[0];
 #pragma unroll
-        for (int r = 1; r < RG; ++r) v += s_red[r * tile_elems + idx];
-        s_red[idx] = v;
+        for (int r = 1; r < RG; ++r) v += r0[r * tile_elems];
+        r0[0] = v;
       }
     }
-    // Split-K over the cluster: every CTA sums a share of the tile over all
-    // ranks' partials in rank order (DSMEM reads), then writes it.
+    // Split-K over the cluster: every CTA sums a share of its tiles over all
+    // ranks' partials in rank order (DSMEM reads), then writes it. The CTAs
+    // of a cluster share blockIdx.x, hence the tiles.
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const unsigned epoch = s_epoch;
     const int rank = (int)cluster.block_rank();
-    for (int idx = rank * T::kThreads + threadIdx.x; idx < tile_elems;
+    for (int idx = rank * T::kThreads + threadIdx.x; idx < n_tl * tile_elems;
          idx += T::kThreads * nsplit) {
+      const int tl = kTiles ? idx / tile_elems : 0, e = idx - tl * tile_elems;
+      const int at = tl * RG * tile_elems + e;
       float v = 0.f;
-      for (int r = 0; r < nsplit; ++r) v += cluster.map_shared_rank(s_red, r)[idx];
-      store_out(p, pp, epi, world, epoch, idx / T::kNT, n0 + idx % T::kNT, v, s_epi[idx]);
+      for (int r = 0; r < nsplit; ++r) v += cluster.map_shared_rank(s_red, r)[at];
+      store_out(p, pp, epi, world, epoch, e / T::kNT, (t_first + tl * t_step) * T::kNT + e % T::kNT, v,
+                s_epi[e]);
     }
     cluster.sync();  // keep this CTA's shared memory alive for the readers
   }
@@ -810,11 +907,24 @@ inline void* gemv_pick_tile(int sw, int rg) {
   }
 }
 
-// Instances by operation set, each table in its own translation unit:
-// plain (w4_gemv.cu), generic (w4_gemv_ops.cu) and the fused decode
+// The plain instances with several tiles per CTA column also come in tiles
+// of 16 compute warps (2 strips x 8 row groups, 4 x 4): one CTA per SM that
+// streams its columns through a deep ring.
+template <bool B, int MB>
+inline void* gemv_pick_stream_tile(int sw, int rg) {
+  switch (sw * 16 + rg) {
+    case 2 * 16 + 8: return gemv_kptr<B, MB, 2, 8, kOpsPlainTiles>();
+    case 4 * 16 + 4: return gemv_kptr<B, MB, 4, 4, kOpsPlainTiles>();
+    default: return gemv_pick_tile<B, MB, kOpsPlainTiles>(sw, rg);
+  }
+}
+
+// Instances by operation set: plain (w4_gemv.cu), generic and plain with
+// several tiles per CTA column (w4_gemv_ops.cu), and the fused decode
 // combinations, bf16 activations with up to 8 batch rows (w4_gemv_fused.cu).
 void* gemv_kernel_plain(int bf16, int mb, int sw, int rg);
 void* gemv_kernel_generic(int bf16, int mb, int sw, int rg);
+void* gemv_kernel_plain_tiles(int bf16, int mb, int sw, int rg);
 void* gemv_kernel_fused(int ops, int sw, int rg);
 
 }  // namespace w4

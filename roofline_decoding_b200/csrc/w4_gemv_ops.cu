@@ -1,7 +1,8 @@
-// w4_gemv_ops.cu - generic instances of the fused W4A16 GEMV: prologue,
-// epilogue and gathered (peer) output chosen at run time. Used for every
+// w4_gemv_ops.cu - generic instances of the fused W4A16 GEMV (prologue,
+// epilogue and gathered (peer) output chosen at run time; used for every
 // combination without an instance of its own, and for the column-parallel
-// gather.
+// gather) and the plain instances whose CTA columns stream several column
+// tiles (large N), including the 16-warp tiles only they have.
 #include "w4_gemv_kernel.cuh"
 
 namespace w4 {
@@ -12,6 +13,12 @@ void* gemv_kernel_generic(int bf16, int mb, int sw, int rg) {
                    : gemv_pick_tile<true, 2, kOpsGeneric>(sw, rg);
   return mb == 1 ? gemv_pick_tile<false, 1, kOpsGeneric>(sw, rg)
                  : gemv_pick_tile<false, 2, kOpsGeneric>(sw, rg);
+}
+
+void* gemv_kernel_plain_tiles(int bf16, int mb, int sw, int rg) {
+  if (bf16)
+    return mb == 1 ? gemv_pick_stream_tile<true, 1>(sw, rg) : gemv_pick_stream_tile<true, 2>(sw, rg);
+  return mb == 1 ? gemv_pick_stream_tile<false, 1>(sw, rg) : gemv_pick_stream_tile<false, 2>(sw, rg);
 }
 
 }  // namespace w4

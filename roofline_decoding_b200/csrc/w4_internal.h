@@ -42,7 +42,11 @@ struct GemvLaunch {
   w4_fused_ops ops;  // zero for a plain GEMV
   const w4_peer_out* peer = nullptr;  // column-parallel: y gathered into every rank's buffer
 };
-size_t gemv_smem_bytes(int M, int K, const w4_gemv_config& cfg);
+size_t gemv_smem_bytes(int M, int K, int N, const w4_gemv_config& cfg);
+// Column tiles covering N, and CTA columns of the launch (cfg.columns, or
+// one per tile when 0 or not below the tile count).
+int gemv_tiles(int N, const w4_gemv_config& cfg);
+int gemv_columns(int N, const w4_gemv_config& cfg);
 int gemv_validate_config(int M, int K, int N, const w4_gemv_config& cfg, const DeviceInfo& di);
 int gemv_choose_config(int M, int K, int N, int split_k, int num_warps, const DeviceInfo& di,
                        w4_gemv_config* out);

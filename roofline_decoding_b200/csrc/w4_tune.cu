@@ -49,7 +49,10 @@ __global__ void fill_halves(uint16_t* p, size_t n, uint64_t seed, float lo, floa
 std::vector<w4_gemv_config> candidates(int M, int K, int N, int split_k, int num_warps, int sms,
                                        const DeviceInfo& di) {
   const int groups = K / 128;
-  std::vector<int> warps = num_warps > 0 ? std::vector<int>{num_warps} : std::vector<int>{4, 8};
+  // 16 compute warps: the streaming tiles (one CTA per SM, several column
+  // tiles per CTA column) only
+  std::vector<int> warps =
+      num_warps > 0 ? std::vector<int>{num_warps} : std::vector<int>{4, 8, 16};
   std::vector<int> splits;
   if (split_k > 0) {
     splits.push_back(split_k);
@@ -61,7 +64,7 @@ std::vector<w4_gemv_config> candidates(int M, int K, int N, int split_k, int num
   auto add = [&](const w4_gemv_config& c) {
     for (const w4_gemv_config& o : out)
       if (o.strips == c.strips && o.row_groups == c.row_groups && o.stages == c.stages &&
-          o.split == c.split)
+          o.split == c.split && o.columns == c.columns)
         return;
     out.push_back(c);
   };
@@ -69,15 +72,33 @@ std::vector<w4_gemv_config> candidates(int M, int K, int N, int split_k, int num
     for (int strips : {1, 2, 4}) {
       const int rg = cw / strips;
       if (rg != 1 && rg != 2 && rg != 4 && rg != 8) continue;
+      if (cw == 16 && strips == 1) continue;
       if (strips > 1 && 32 * strips > N) continue;
       const int tiles = (N + 32 * strips - 1) / (32 * strips);
       for (int split : splits) {
-        if (split_k <= 0 && split > 1 && tiles * split > 6 * sms) continue;
-        const int gps = (groups + split - 1) / split;
-        const int n_stages = (gps + rg - 1) / rg;
-        for (int stages : {2, 3, 4, 5, 6, 8}) {
-          if (stages > std::max(2, n_stages)) continue;
-          add(w4_gemv_config{strips, rg, stages, split, 0});
+        // one CTA per column tile (0), and for large N grids of one or two
+        // CTAs per SM in all, each CTA column streaming two or more tiles
+        int col_opts[3] = {0, 0, 0};
+        int n_col = 1;
+        for (int per_sm = 1; per_sm <= 2; ++per_sm) {
+          const int c = std::max(1, (per_sm * sms + split / 2) / split);
+          if (2 * c <= tiles && c != col_opts[n_col - 1]) col_opts[n_col++] = c;
+        }
+        for (int ci = 0; ci < n_col; ++ci) {
+          const int columns = col_opts[ci];
+          if (cw == 16 && (columns == 0 || columns * split > sms + split)) continue;
+          const int ctas = (columns ? columns : tiles) * split;
+          if (split_k <= 0 && split > 1 && ctas > 6 * sms) continue;
+          const int gps = (groups + split - 1) / split;
+          const int per_col = columns ? (tiles + columns - 1) / columns : 1;
+          const int n_stages = (gps + rg - 1) / rg * per_col;
+          for (int stages : {2, 3, 4, 5, 6, 8}) {
+            if (stages > std::max(2, n_stages)) continue;
+            if (columns && ((stages != 4 && stages != 6) ||
+                            (split != 1 && split != 2 && split != 4 && split != 8)))
+              continue;  // a streaming ring: fewer depths to try
+            add(w4_gemv_config{strips, rg, stages, split, 0, columns});
+          }
         }
       }
     }

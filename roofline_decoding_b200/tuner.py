@@ -18,37 +18,56 @@ import torch
 from ._lib import GemvConfig
 
 
+def column_options(tiles: int, split: int, sm_count: int) -> list[int]:
+    """CTA-column counts to try: one CTA per tile (0), and for large N grids
+    of one or two CTAs per SM in total (columns * split), each CTA column
+    streaming two or more tiles back to back."""
+    out = [0]
+    for per_sm in (1, 2):
+        c = max(1, (per_sm * sm_count + split // 2) // split)
+        if 2 * c <= tiles and c not in out:
+            out.append(c)
+    return out
+
+
 def _candidates(M: int, K: int, N: int, split_k: int | None, num_warps: int | None,
                 sm_count: int):
     from .kernels import default_config
 
     groups = K // 128
-    warps = [num_warps] if num_warps else [4, 8]
+    # 16 compute warps: the streaming tiles (one CTA per SM, several column
+    # tiles per CTA column) only
+    warps = [num_warps] if num_warps else [4, 8, 16]
     splits = [split_k] if split_k else [s for s in (1, 2, 3, 4, 6, 8, 12, 16) if s <= groups]
     seen = set()
     for cw in warps:
         for strips in (1, 2, 4):
             rg = cw // strips
-            if rg not in (1, 2, 4, 8):
+            if rg not in (1, 2, 4, 8) or (cw == 16 and strips == 1):
                 continue
             if strips > 1 and 32 * strips > N:
                 continue
             tiles = -(-N // (32 * strips))
             for split in splits:
-                ctas = tiles * split
-                if not split_k and split > 1 and ctas > 6 * sm_count:
-                    continue  # already plenty of CTAs without splitting further
-                gps = -(-groups // split)
-                n_stages = -(-gps // rg)
-                # up to the whole share in flight at once (small shapes are latency
-                # bound: every stage that waits for a free slot costs a DRAM trip)
-                for stages in (2, 3, 4, 5, 6, 8):
-                    if stages > max(2, n_stages):
-                        continue
-                    c = (strips, rg, stages, split, 0)
-                    if c not in seen:
-                        seen.add(c)
-                        yield GemvConfig(*c)
+                for columns in column_options(tiles, split, sm_count):
+                    if cw == 16 and (not columns or columns * split > sm_count + split):
+                        continue  # 16-warp tiles: one CTA per SM, several tiles each
+                    ctas = (columns or tiles) * split
+                    if not split_k and split > 1 and ctas > 6 * sm_count:
+                        continue  # already plenty of CTAs without splitting further
+                    gps = -(-groups // split)
+                    n_stages = -(-gps // rg) * (-(-tiles // columns) if columns else 1)
+                    # up to the whole share in flight at once (small shapes are latency
+                    # bound: every stage that waits for a free slot costs a DRAM trip)
+                    for stages in (2, 3, 4, 5, 6, 8):
+                        if stages > max(2, n_stages):
+                            continue
+                        if columns and (stages not in (4, 6) or split not in (1, 2, 4, 8)):
+                            continue  # a streaming ring: fewer depths to try
+                        c = (strips, rg, stages, split, 0) + ((columns,) if columns else ())
+                        if c not in seen:
+                            seen.add(c)
+                            yield GemvConfig(*c)
     d = default_config(M, K, N, split_k or 0, num_warps or 0)
     if d.as_tuple() not in seen:
         yield d

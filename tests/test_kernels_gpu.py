@@ -260,6 +260,45 @@ def test_gemv_every_tile(strips, row_groups, stages):
     check_gemv(2048, 640, config=cfg)
 
 
+@pytest.mark.parametrize("strips,row_groups,stages,split,columns",
+                         [(1, 8, 4, 1, 40), (1, 8, 6, 2, 64), (2, 4, 4, 4, 5), (4, 2, 4, 1, 5),
+                          (1, 4, 4, 8, 9), (4, 1, 4, 2, 3), (2, 2, 6, 1, 7), (2, 1, 4, 4, 1)])
+@pytest.mark.parametrize("M,bf16", [(1, False), (3, True), (9, False)])
+def test_gemv_several_tiles_per_cta_column(strips, row_groups, stages, split, columns, M, bf16):
+    """CTA columns streaming several column tiles back to back (the large-N
+    grids): uneven tile counts per column, a ragged last tile (N = 4104), split
+    K over clusters and a column that takes every tile."""
+    cfg = GemvConfig(strips, row_groups, stages, split, 0, columns)
+    check_gemv(2048, 4104, M=M, bf16=bf16, config=cfg, seed=columns)
+
+
+@pytest.mark.parametrize("strips,row_groups,stages,split,columns",
+                         [(2, 8, 4, 1, 20), (4, 4, 4, 2, 5), (2, 8, 3, 2, 33)])
+@pytest.mark.parametrize("M,bf16", [(1, True), (3, False)])
+def test_gemv_sixteen_warp_streaming_tiles(strips, row_groups, stages, split, columns, M, bf16):
+    """The 16-compute-warp tiles, which exist only for CTA columns that stream
+    several column tiles."""
+    cfg = GemvConfig(strips, row_groups, stages, split, 0, columns)
+    check_gemv(2048, 4104, M=M, bf16=bf16, config=cfg, seed=columns)
+    with pytest.raises(ValueError):  # one tile per CTA: no such instance
+        check_gemv(2048, 4104, M=M, bf16=bf16, config=GemvConfig(strips, row_groups, stages, 1, 0))
+
+
+def test_several_tiles_per_cta_column_needs_a_plain_output():
+    """An epilogue reads operands per tile: with fewer CTA columns than tiles
+    the launch is refused, not run."""
+    from roofline_decoding_b200 import _lib
+    p, s = pack_dev(gen(1024, 1024))
+    x = torch.randn(1, 1024, device=DEV).half()
+    y = torch.empty(1, 1024, device=DEV).half()
+    bias = torch.zeros(1024, device=DEV).half()
+    with pytest.raises(NotImplementedError):
+        K.fused_launch(x, p, s, y, GemvConfig(1, 8, 4, 1, 0, 4), epilogue=_lib.W4_EPI_BIAS,
+                       epi_src=bias)
+    K.fused_launch(x, p, s, y, GemvConfig(1, 8, 4, 1, 0, 4), _lib.W4_PRO_RMSNORM,
+                   torch.ones(1024, device=DEV).half())  # a prologue is per CTA: allowed
+
+
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 7, 8, 9, 12, 16])
 @pytest.mark.parametrize("bf16", [False, True])
 def test_small_m_gemm(M, bf16):
