@@ -97,11 +97,10 @@ WORKLOADS = {
 NCU_TRAFFIC = {
     (1, 1536, 8960): 7_140_096,
     (1, 8960, 1536): 7_154_944,
-    # profiles/w4_gemv_kernel_large_8192x28672.md: one launch of tile (4, 2, 3, 1)
-    (1, 8192, 28672): 125_276_160,
-    # the same kernel instance (tile and K) over 1002 column tiles instead of
-    # 224: the capture above scaled by the column tiles processed
-    (1, 8192, 128256): 560_387_108,
+    # profiles/w4_gemv_kernel_stream_8192x128256_8192x28672.md: one launch each
+    # of the tuned streaming tiles
+    (1, 8192, 28672): 124_964_352,
+    (1, 8192, 128256): 545_657_088,
 }
 
 

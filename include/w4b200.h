@@ -208,6 +208,14 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed,
  * aligned. */
 int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scales,
             void* y, int y_dtype, int M, int K, int N, void* stream);
+/* Same, with the K split fixed: split_k = 0 lets the library choose (grids of
+ * fewer tiles than SMs cut K into slices; a last wave of a few tiles goes to a
+ * second, programmatically dependent launch of K-sliced tiles), 1..8 runs one
+ * launch of 128-column tiles with K cut into that many slices (<= K/64).
+ * The slices of a tile form a cluster and are summed over DSMEM in rank
+ * order: results do not depend on scheduling. */
+int w4_gemm_ex(const void* x, int x_dtype, const int32_t* packed, const void* scales,
+               void* y, int y_dtype, int M, int K, int N, int split_k, void* stream);
 
 /* Calibrated int4 packing (GPTQ), the step the reference lists after its
  * round-to-nearest packer (devto_article.md:71), in the same packed format

@@ -139,6 +139,8 @@ SIGNATURES = {
     "w4_decode_step": (_c_int, [ctypes.POINTER(DecodeModel), _c_void_p, _c_size_t, _c_void_p]),
     "w4_gemm": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int,
                          _c_int, _c_int, _c_void_p]),
+    "w4_gemm_ex": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int,
+                            _c_int, _c_int, _c_int, _c_void_p]),
     "w4_gptq_block": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p,
                                _c_void_p]),
     "w4_gemv_tune": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,

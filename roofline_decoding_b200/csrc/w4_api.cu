@@ -325,7 +325,15 @@ int w4_gemv_fused(const void* x, int x_dtype, const int32_t* packed, const void*
 
 int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scales, void* y,
             int y_dtype, int M, int K, int N, void* stream) {
+  return w4_gemm_ex(x, x_dtype, packed, scales, y, y_dtype, M, K, N, 0, stream);
+}
+
+int w4_gemm_ex(const void* x, int x_dtype, const int32_t* packed, const void* scales, void* y,
+               int y_dtype, int M, int K, int N, int split_k, void* stream) {
   if (!x || !packed || !scales || !y) return fail(W4_ERR_INVALID_ARG, "w4_gemm: null pointer");
+  if (split_k < 0 || split_k > 8 || (split_k > 0 && split_k > K / 64))
+    return fail(W4_ERR_INVALID_ARG, "w4_gemm: split_k=%d (0 = choose, else 1..8 and <= K/64)",
+                split_k);
   int st = check_dtype(x_dtype, "w4_gemm x");
   if (st != W4_OK) return st;
   if ((st = check_dtype(y_dtype, "w4_gemm y")) != W4_OK) return st;
@@ -335,7 +343,7 @@ int w4_gemm(const void* x, int x_dtype, const int32_t* packed, const void* scale
   if (!aligned16(x) || !aligned16(packed) || !aligned16(scales) || !aligned16(y))
     return fail(W4_ERR_ALIGNMENT, "w4_gemm: pointers must be 16-byte aligned");
   return launch_gemm(x, x_dtype == W4_BF16, packed, scales, y, y_dtype == W4_BF16, M, K, N,
-                     (cudaStream_t)stream);
+                     split_k, (cudaStream_t)stream);
 }
 
 int w4_gptq_block(const float* w, const float* hinv, int N, int32_t* packed, void* scales,

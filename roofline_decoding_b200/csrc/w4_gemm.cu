@@ -24,10 +24,24 @@
 // fp32 product; the reference has no bf16 path). Every wait is bounded; a
 // CTA that gives up sets the device error word, drains its copies and
 // frees its tensor memory.
+//
+// Work split: a launch covers a region of output tiles in row-major order
+// (blockIdx.x) and may cut K into up to 16 slices (blockIdx.z), the slices of
+// a tile forming a thread-block cluster. A sliced CTA leaves its fp32
+// accumulators in shared memory (the freed operand rings) and every rank then
+// sums a band of the tile's rows over all ranks in rank order (DSMEM), so the
+// result does not depend on scheduling. The host uses slices for grids of
+// too few tiles, and for the last few tiles of a grid that would otherwise
+// leave most SMs idle in a final wave (a second, programmatically dependent
+// launch that runs while the first one's last wave finishes).
 #include "w4_internal.h"
 #include "w4_ptx.cuh"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
+
+namespace cg = cooperative_groups;
 
 namespace w4 {
 
@@ -36,12 +50,10 @@ namespace {
 constexpr int kUM = 128;          // MMA M (rows of one accumulator)
 constexpr int kBMMax = 2 * kUM;   // rows of Y per CTA: up to two accumulators share a W tile
 constexpr int kBK = 64;           // k per ring stage (one 128-byte swizzle row of fp16)
-constexpr int kStages = 3;        // TMA ring
 constexpr int kBStages = 3;       // dequantised W buffers
 constexpr int kDqWarps = 8;       // dequant (and epilogue) warps
 constexpr int kMmaWarp = 1 + kDqWarps;
 constexpr int kGemmThreads = 32 * (kMmaWarp + 1);  // warp 0 TMA, 1..8 dequant, 9 MMA
-constexpr int kNumBars = 2 * kStages + 2 * kBStages + 1;
 constexpr int kErrGemmWait = 7;
 
 struct GemmParams {
@@ -49,6 +61,12 @@ struct GemmParams {
   int M, K, N;
   int x_bf16, y_bf16;
   int* err;
+  // output tiles of this launch: blockIdx.x = t is tile (m_tile0 + t / ntx,
+  // n_tile0 + t % ntx) in units of the instance's rows and columns
+  int m_tile0, n_tile0, ntx;
+  int ksplit;       // K slices (gridDim.z, one cluster per tile when > 1)
+  int wait_at_end;  // a launch overlapping the previous one on the stream
+                    // completes only after it (griddepcontrol.wait at exit)
 };
 
 // Tile of BN columns (MMA N = BN, 128 or 256) and its shared memory layout
@@ -56,6 +74,10 @@ struct GemmParams {
 // barriers and the tensor-memory address.
 template <int BN, int NACC>
 struct GemmShape {
+  // TMA ring: 3 slots of 32 KB X tiles with two accumulators; 4 slots of
+  // 16 KB with one (the same bytes in flight, one more stage of latency cover)
+  static constexpr int kStages = NACC == 1 ? 4 : 3;
+  static constexpr int kNumBars = 2 * kStages + 2 * kBStages + 1;
   static constexpr int kBM = NACC * kUM;                 // rows of Y per CTA
   static constexpr int kXBytes = kBM * kBK * 2;          // 16 or 32 KB
   static constexpr int kBBytes = BN * kBK * 2;           // 16 or 32 KB
@@ -77,6 +99,10 @@ struct GemmShape {
                     kScBytes % 128 == 0,
                 "tensor-copy destinations are 128-byte aligned");
   static_assert(kTmemCols <= 512 && kWordsPerThread * kThreadsPerCol == kBK / 8, "tile");
+  // K slices: the fp32 partial tile (rows padded by 4 floats against bank
+  // conflicts) reuses the X and B rings, free once the accumulators are final
+  static constexpr int kPitch = BN + 4;
+  static constexpr bool kCanSplit = kBM * kPitch * 4 <= kOffPk;
 };
 
 // ---------------------------------------------------------------- tcgen05
@@ -201,20 +227,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_gemm) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + S::kOffBar);
   uint64_t* full_tma = bars;                       // X + packed + scales landed
-  uint64_t* empty_tma = full_tma + kStages;        // dequant read the words, MMA read X
-  uint64_t* full_b = empty_tma + kStages;          // B buffer written
+  uint64_t* empty_tma = full_tma + S::kStages;        // dequant read the words, MMA read X
+  uint64_t* full_b = empty_tma + S::kStages;          // B buffer written
   uint64_t* empty_b = full_b + kBStages;           // MMA read the B buffer
   uint64_t* acc_full = empty_b + kBStages;         // accumulator final
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S::kOffTmem);
   int* abort_flag = reinterpret_cast<int*>(base + S::kOffTmem + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * S::kBM;
-  const int KT = p.K / kBK;
-  constexpr int kt0 = 0;
+  const int t = (int)blockIdx.x;
+  const int n0 = (p.n_tile0 + t % p.ntx) * BN, m0 = (p.m_tile0 + t / p.ntx) * S::kBM;
+  // this CTA's K slice: 64-k stages [kt0, kt0 + KT)
+  const int KT_all = p.K / kBK;
+  const int kt0 = (int)((long long)blockIdx.z * KT_all / p.ksplit);
+  const int KT = (int)((long long)(blockIdx.z + 1) * KT_all / p.ksplit) - kt0;
+  grid_launch_dependents();  // a dependent launch may fill the SMs this grid frees
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < S::kStages; ++i) {
       mbar_init(&full_tma[i], 1);
       mbar_init(&empty_tma[i], kDqWarps + 1);  // the dequant warps + the MMA commit
     }
@@ -251,8 +281,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tma_prefetch_desc(&tm_s);
       int issued = 0;
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kStages;
-        if (kt >= kStages && !mbar_wait(&empty_tma[s], ((kt / kStages) & 1) ^ 1u)) {
+        const int s = kt % S::kStages;
+        if (kt >= S::kStages && !mbar_wait(&empty_tma[s], ((kt / S::kStages) & 1) ^ 1u)) {
           give_up(kErrGemmWait);
           break;
         }
@@ -264,8 +294,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tma_load_2d(base + S::kOffSc + s * S::kScBytes, &tm_s, &full_tma[s], n0, (kg * kBK) / 128);
         ++issued;
       }
-      for (int j = issued - kStages > 0 ? issued - kStages : 0; j < issued; ++j)
-        if (!mbar_wait(&full_tma[j % kStages], (j / kStages) & 1)) give_up(kErrDrainWait);
+      for (int j = issued - S::kStages > 0 ? issued - S::kStages : 0; j < issued; ++j)
+        if (!mbar_wait(&full_tma[j % S::kStages], (j / S::kStages) & 1)) give_up(kErrDrainWait);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA
@@ -273,8 +303,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       constexpr uint32_t idesc = f16_idesc(kBF16 ? 1 : 0, kUM, BN);
       int done = 0;
       for (int kt = 0; kt < KT && !stopped(); ++kt) {
-        const int s = kt % kStages, sb = kt % kBStages;
-        if (!mbar_wait(&full_tma[s], (kt / kStages) & 1) ||
+        const int s = kt % S::kStages, sb = kt % kBStages;
+        if (!mbar_wait(&full_tma[s], (kt / S::kStages) & 1) ||
             !mbar_wait(&full_b[sb], (kt / kBStages) & 1)) {
           give_up(kErrGemmWait);
           break;
@@ -305,8 +335,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int n = dt % BN;                                  // column of the tile
     const int jh = (dt / BN) * S::kWordsPerThread;          // this thread's words of the column
     for (int kt = 0; kt < KT && !stopped(); ++kt) {
-      const int s = kt % kStages, sb = kt % kBStages;
-      if (!mbar_wait(&full_tma[s], (kt / kStages) & 1) ||
+      const int s = kt % S::kStages, sb = kt % kBStages;
+      if (!mbar_wait(&full_tma[s], (kt / S::kStages) & 1) ||
           (kt >= kBStages && !mbar_wait(&empty_b[sb], ((kt / kBStages) & 1) ^ 1u))) {
         give_up(kErrGemmWait);
         break;
@@ -333,7 +363,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ epilogue
     if (!mbar_wait(acc_full, 0)) give_up(kErrGemmWait);
     tc_fence_after();
-    if (!stopped()) {
+    if (p.ksplit > 1) {
+      // K slice: this warp's 32 rows of its accumulator -> the fp32 partial tile
+      if constexpr (S::kCanSplit) {
+        const int q = warp & 3, half = (warp - 1) / 4;
+        if (!stopped() && half < NACC) {
+          float* prow = reinterpret_cast<float*>(base) + (size_t)(half * kUM + 32 * q + lane) * S::kPitch;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem_d + ((uint32_t)(32 * q) << 16) + half * BN + 32 * c, r);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              *reinterpret_cast<uint4*>(prow + 32 * c + 4 * v) =
+                  make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+        }
+      }
+    } else if (!stopped()) {
       const int q = warp & 3;            // this warp's 32-lane slice of tensor memory
       const int half = (warp - 1) / 4;   // which accumulator (rows 0..127 or 128..255)
       if (half >= NACC) goto epilogue_done;
@@ -370,6 +417,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
+  if constexpr (S::kCanSplit) {
+    if (p.ksplit > 1) {
+      // rank r writes rows [r*R/S, (r+1)*R/S) of the tile, each the sum of
+      // every rank's partial in rank order
+      cg::cluster_group cluster = cg::this_cluster();
+      cluster.sync();
+      const int rank = (int)blockIdx.z;
+      const int r0 = rank * S::kBM / p.ksplit, r1 = (rank + 1) * S::kBM / p.ksplit;
+      constexpr int kC4 = BN / 4;
+      const float* part = reinterpret_cast<const float*>(base);
+      for (int i = threadIdx.x; i < (r1 - r0) * kC4; i += kGemmThreads) {
+        const int row = r0 + i / kC4, c4 = i - (i / kC4) * kC4;
+        const int at = row * S::kPitch + 4 * c4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int rr = 0; rr < p.ksplit; ++rr) {
+          const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(part + at, rr));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        const int grow = m0 + row, gcol = n0 + 4 * c4;
+        if (grow < p.M && gcol < p.N) {
+          uint2 o;
+          if (p.y_bf16) {
+            const __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y);
+            const __nv_bfloat162 b = __floats2bfloat162_rn(acc.z, acc.w);
+            o = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                           *reinterpret_cast<const uint32_t*>(&b));
+          } else {
+            const __half2 a = __floats2half2_rn(acc.x, acc.y);
+            const __half2 b = __floats2half2_rn(acc.z, acc.w);
+            o = make_uint2(*reinterpret_cast<const uint32_t*>(&a),
+                           *reinterpret_cast<const uint32_t*>(&b));
+          }
+          *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.y) + (size_t)grow * p.N + gcol) = o;
+        }
+      }
+      cluster.sync();  // the other ranks' reads of this CTA's partial are done
+    }
+  }
   if (warp == kMmaWarp) {
     // every MMA has completed (acc_full) before its tensor memory is freed
     if (lane == 0 && !mbar_wait(acc_full, 0)) give_up(kErrGemmWait);
@@ -379,6 +467,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  "r"(S::kTmemCols)
                  : "memory");
   }
+  if (p.wait_at_end) grid_dependency_wait();
 }
 
 bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem, const void* gaddr,
@@ -406,8 +495,10 @@ int gemm_init_device(const DeviceInfo& di) {
   struct K {
     void* fn;
     int smem;
-  } ks[6] = {{gemm_fn<false, 128, 1>(), GemmShape<128, 1>::kSmem},
+  } ks[8] = {{gemm_fn<false, 128, 1>(), GemmShape<128, 1>::kSmem},
              {gemm_fn<true, 128, 1>(), GemmShape<128, 1>::kSmem},
+             {gemm_fn<false, 256, 1>(), GemmShape<256, 1>::kSmem},
+             {gemm_fn<true, 256, 1>(), GemmShape<256, 1>::kSmem},
              {gemm_fn<false, 128, 2>(), GemmShape<128, 2>::kSmem},
              {gemm_fn<true, 128, 2>(), GemmShape<128, 2>::kSmem},
              {gemm_fn<false, 256, 2>(), GemmShape<256, 2>::kSmem},
@@ -436,49 +527,136 @@ static int gemm_tile(int M, int N, int sms, int* nacc) {
   return 128;
 }
 
+namespace {
+
+// One launch of a prepared plan: the instance, its tile region and K slices.
+struct GemmLaunch {
+  int bn, nacc;
+  int m_tile0, n_tile0, ntx, tiles;
+  int ksplit;
+  bool after_previous;  // programmatic dependent launch, waits for it at exit
+};
+
+void* gemm_instance(int bf16, int bn, int nacc, size_t* smem) {
+  if (bn == 256 && nacc == 2) {
+    *smem = GemmShape<256, 2>::kSmem;
+    return bf16 ? gemm_fn<true, 256, 2>() : gemm_fn<false, 256, 2>();
+  }
+  if (bn == 256) {
+    *smem = GemmShape<256, 1>::kSmem;
+    return bf16 ? gemm_fn<true, 256, 1>() : gemm_fn<false, 256, 1>();
+  }
+  if (nacc == 2) {
+    *smem = GemmShape<128, 2>::kSmem;
+    return bf16 ? gemm_fn<true, 128, 2>() : gemm_fn<false, 128, 2>();
+  }
+  *smem = GemmShape<128, 1>::kSmem;
+  return bf16 ? gemm_fn<true, 128, 1>() : gemm_fn<false, 128, 1>();
+}
+
+// The launches of one GEMM (at most two). split_k > 0 forces one launch of
+// 128 x 256 tiles (one accumulator) cut into that many K slices.
+int gemm_plan(int M, int K, int N, int sms, int split_k, GemmLaunch* out) {
+  const int kt = K / kBK;
+  const int nt128 = (N + 127) / 128;
+  // the K-sliced tile: 128 rows x 256 columns (its partial tile fits the
+  // freed rings; two accumulators of 256 columns would not)
+  const int nt256 = (N + 255) / 256, mt1 = (M + kUM - 1) / kUM;
+  if (split_k > 0) {
+    out[0] = GemmLaunch{256, 1, 0, 0, nt256, nt256 * mt1, std::min(split_k, kt), false};
+    return 1;
+  }
+  int nacc = 2;
+  const int bn = gemm_tile(M, N, sms, &nacc);
+  const int bm = nacc * kUM;
+  const int ntx = (N + bn - 1) / bn, mtx = (M + bm - 1) / bm;
+  const int tiles = ntx * mtx;
+  // A grid of fewer tiles than SMs is not cut along K: measured on 2048 x
+  // 8960 x 1536 (96 tiles), three K slices over 288 CTAs took 118-128 us
+  // against 96 us for the 96 whole tiles (each slice's stages ran at half the
+  // rate).
+  if (tiles >= sms && bn == 256 && nacc == 2) {
+    // a last wave of a few tiles: those tiles go to a second launch as
+    // 128-column tiles cut into K slices, spread over the SMs the first
+    // launch frees
+    const int rem = tiles % sms;
+    if (rem > 0 && rem * 4 <= sms && rem <= ntx) {
+      const int n_lo = (ntx - rem) * 2;  // first 128-column tile of the remainder
+      const int nrx = nt128 - n_lo;
+      const int s = std::max(1, std::min(8, std::min(sms / nrx, kt / 4)));
+      out[0] = GemmLaunch{256, 2, 0, 0, ntx, tiles - rem, 1, false};
+      out[1] = GemmLaunch{128, 2, mtx - 1, n_lo, nrx, nrx, s, true};
+      return 2;
+    }
+  }
+  out[0] = GemmLaunch{bn, nacc, 0, 0, ntx, tiles, 1, false};
+  return 1;
+}
+
+}  // namespace
+
 int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
-                int y_bf16, int M, int K, int N, cudaStream_t stream) {
+                int y_bf16, int M, int K, int N, int split_k, cudaStream_t stream) {
   int dev = 0;
   int st = current_device(&dev);
   if (st != W4_OK) return st;
   const DeviceInfo& di = device_info(dev);
-  int nacc = 2;
-  const int BN = gemm_tile(M, N, di.sm_count > 0 ? di.sm_count : 148, &nacc);
-  const int BM = nacc * kUM;
-  CUtensorMap tm_x, tm_w, tm_s;
-  if (!encode_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                 2, x, (uint64_t)K, (uint64_t)M, kBK, (uint32_t)BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, packed, (uint64_t)N, (uint64_t)(K / 8),
-                 (uint32_t)BN, kBK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, (uint64_t)N,
-                 (uint64_t)(K / 128), (uint32_t)BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return fail(W4_ERR_CUDA, "cuTensorMapEncodeTiled failed for w4_gemm M=%d K=%d N=%d", M, K, N);
-  GemmParams p;
-  p.y = y;
-  p.M = M;
-  p.K = K;
-  p.N = N;
-  p.x_bf16 = x_bf16;
-  p.y_bf16 = y_bf16;
-  p.err = di.err_word;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), 1);
-  cfg.blockDim = dim3(kGemmThreads);
-  cfg.stream = stream;
-  void* fn;
-  if (BN == 256) {
-    cfg.dynamicSmemBytes = GemmShape<256, 2>::kSmem;
-    fn = x_bf16 ? gemm_fn<true, 256, 2>() : gemm_fn<false, 256, 2>();
-  } else if (nacc == 2) {
-    cfg.dynamicSmemBytes = GemmShape<128, 2>::kSmem;
-    fn = x_bf16 ? gemm_fn<true, 128, 2>() : gemm_fn<false, 128, 2>();
-  } else {
-    cfg.dynamicSmemBytes = GemmShape<128, 1>::kSmem;
-    fn = x_bf16 ? gemm_fn<true, 128, 1>() : gemm_fn<false, 128, 1>();
+  GemmLaunch plan[2];
+  const int n = gemm_plan(M, K, N, di.sm_count > 0 ? di.sm_count : 148, split_k, plan);
+  for (int i = 0; i < n; ++i) {
+    const GemmLaunch& L = plan[i];
+    const int BM = L.nacc * kUM;
+    CUtensorMap tm_x, tm_w, tm_s;
+    if (!encode_2d(&tm_x,
+                   x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   x, (uint64_t)K, (uint64_t)M, kBK, (uint32_t)BM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&tm_w, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, packed, (uint64_t)N,
+                   (uint64_t)(K / 8), (uint32_t)L.bn, kBK / 8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(&tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, scales, (uint64_t)N,
+                   (uint64_t)(K / 128), (uint32_t)L.bn, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return fail(W4_ERR_CUDA, "cuTensorMapEncodeTiled failed for w4_gemm M=%d K=%d N=%d", M, K,
+                  N);
+    GemmParams p;
+    p.y = y;
+    p.M = M;
+    p.K = K;
+    p.N = N;
+    p.x_bf16 = x_bf16;
+    p.y_bf16 = y_bf16;
+    p.err = di.err_word;
+    p.m_tile0 = L.m_tile0;
+    p.n_tile0 = L.n_tile0;
+    p.ntx = L.ntx;
+    p.ksplit = L.ksplit;
+    p.wait_at_end = L.after_previous ? 1 : 0;
+    size_t smem = 0;
+    void* fn = gemm_instance(x_bf16, L.bn, L.nacc, &smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)L.tiles, 1, (unsigned)L.ksplit);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    unsigned na = 0;
+    if (L.ksplit > 1) {
+      attrs[na].id = cudaLaunchAttributeClusterDimension;
+      attrs[na].val.clusterDim.x = 1;
+      attrs[na].val.clusterDim.y = 1;
+      attrs[na].val.clusterDim.z = (unsigned)L.ksplit;
+      ++na;
+    }
+    if (L.after_previous) {
+      attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attrs[na].val.programmaticStreamSerializationAllowed = 1;
+      ++na;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = na;
+    void* args[] = {&tm_x, &tm_w, &tm_s, &p};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+    if (e != cudaSuccess) return cuda_fail(e, "w4_gemm launch");
   }
-  void* args[] = {&tm_x, &tm_w, &tm_s, &p};
-  cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
-  return e == cudaSuccess ? W4_OK : cuda_fail(e, "w4_gemm launch");
+  return W4_OK;
 }
 
 }  // namespace w4

@@ -86,7 +86,7 @@ inline bool lm_head_hidden_supported(int hidden) {
 // tcgen05 W4A16 GEMM (w4_gemm.cu).
 int gemm_init_device(const DeviceInfo& di);
 int launch_gemm(const void* x, int x_bf16, const int32_t* packed, const void* scales, void* y,
-                int y_bf16, int M, int K, int N, cudaStream_t stream);
+                int y_bf16, int M, int K, int N, int split_k, cudaStream_t stream);
 
 // Calibrated (GPTQ) packing, one 128-row block (w4_gptq.cu).
 int gptq_init_device(const DeviceInfo& di);

@@ -85,6 +85,13 @@ class W4DecodeModel:
     # second half of a tile, so gate and up alternate in blocks of half a tile.
     GU_CONFIG = (2, 4, 2, 1, 0)
     GU_BLOCK = 16 * GU_CONFIG[0]
+    # Tiles of the fused step's other GEMVs, keyed by (K, N), chosen by timing
+    # whole captured steps of the Qwen2.5-1.5B architecture (bf16): inside a
+    # step they share the SMs with the kernels around them, and the tile that
+    # wins a chain of the GEMV alone can lose there (o: (1, 4, 3) took the step
+    # from 0.721 to 0.766 ms). Other shapes use the tuned tile.
+    STEP_TILES = {(1536, 2048): (1, 8, 2, 1, 0), (1536, 1536): (1, 8, 2, 1, 0),
+                  (8960, 1536): (1, 8, 2, 8, 0)}
 
     @staticmethod
     def interleave_gate_up(w: torch.Tensor, block: int) -> torch.Tensor:
@@ -275,6 +282,8 @@ class W4DecodeModel:
             out = {}
             for name, (K, N) in shapes.items():
                 c = tuned_config(1, K, N, bf, bf, None, None, self.device)
+                if self.mode == "fused" and (K, N) in self.STEP_TILES:
+                    c = GemvConfig(*self.STEP_TILES[(K, N)])
                 if name == "gu" and self.gu_block:
                     c = GemvConfig(*self.GU_CONFIG)  # the tile the columns are interleaved for
                 out[name] = c.with_pdl(1 if self.pdl else 0)

@@ -403,13 +403,16 @@ def gemv_v3(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, split_k
 
 
 def w4_gemm(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
-            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+            out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+            split_k: int | None = None) -> torch.Tensor:
     """y = x @ dequantize_v1(packed, scales) on the tensor cores for any number of rows.
 
     The prefill path of W4Linear: the reference dequantises to an fp16 [K, N]
     copy and runs an fp32 matmul (scripts/decode_loop.py:51-55); this kernel
     dequantises tile by tile into shared memory and accumulates in fp32 with
     tcgen05. x is [M, K] (or [K]) fp16 or bf16; N must be a multiple of 128.
+    split_k: None lets the library cut K where the tiles do not fill the GPU;
+    1..8 forces one launch with K in that many slices (summed in a fixed order).
     """
     K, N = _check_packed(packed, scales)
     if N % 128:
@@ -427,9 +430,10 @@ def w4_gemm(x: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor,
         y = out
     lib = _lib.load()
     with _on_device(packed.device):
-        _lib.check(lib.w4_gemm(x2.data_ptr(), _DTYPE_CODE[x2.dtype], packed.contiguous().data_ptr(),
-                               scales.contiguous().data_ptr(), y.data_ptr(), _DTYPE_CODE[y_dtype],
-                               M, K, N, _stream_ptr(packed.device)), "w4_gemm")
+        _lib.check(lib.w4_gemm_ex(x2.data_ptr(), _DTYPE_CODE[x2.dtype],
+                                  packed.contiguous().data_ptr(), scales.contiguous().data_ptr(),
+                                  y.data_ptr(), _DTYPE_CODE[y_dtype], M, K, N, int(split_k or 0),
+                                  _stream_ptr(packed.device)), "w4_gemm")
     if out is not None:
         return out
     return y[0] if squeeze else y

@@ -91,3 +91,54 @@ def test_gemm_rejects_bad_shapes():
     p2, s2 = Kn.pack_weights((torch.randn(256, 200) * 0.02).half().cuda())
     with pytest.raises(ValueError):
         Kn.w4_gemm(x.cuda(), p2, s2)
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 1024, 384), (129, 2048, 640), (100, 512, 256),
+                                   (1024, 1536, 1536)])
+@pytest.mark.parametrize("split_k", [2, 3, 5, 8])
+def test_gemm_k_slices_match_oracle(M, K, N, split_k):
+    """K cut into slices (128 x 256 tiles, a cluster per tile, partials summed
+    over DSMEM in rank order), including slice counts that do not divide the
+    64-k stages and a last tile half outside N."""
+    x, packed, scales = _case(M, K, N, seed=M + split_k)
+    y = Kn.w4_gemm(x.cuda(), packed, scales, split_k=split_k).float().cpu()
+    want = _want(x, packed, scales)
+    assert torch.allclose(y, want.half().float(), rtol=4e-3, atol=4e-3), \
+        (y - want).abs().max().item()
+    y2 = Kn.w4_gemm(x.cuda(), packed, scales, split_k=split_k).float().cpu()
+    assert torch.equal(y, y2)  # a fixed summation order
+    assert Kn.device_error() == 0
+
+
+def test_gemm_k_slices_bf16():
+    x, packed, scales = _case(257, 2048, 512, seed=4, x_dtype=torch.bfloat16)
+    y = Kn.w4_gemm(x.cuda(), packed, scales, split_k=4).float().cpu()
+    want = _want(x, packed, scales, bf16_weights=True)
+    assert torch.allclose(y, want, rtol=2e-2, atol=2e-2), (y - want).abs().max().item()
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (512, 4096, 1536),   # 24 tiles of 256 x 128, fewer than the SMs: one launch
+    (1000, 512, 9728),   # 152 tiles of 256 x 256: 148 in one launch, 4 in a K-sliced second
+])
+def test_gemm_library_split_choices_match_oracle(M, K, N):
+    x, packed, scales = _case(M, K, N, seed=K)
+    y = Kn.w4_gemm(x.cuda(), packed, scales).float().cpu()
+    want = _want(x, packed, scales)
+    assert torch.allclose(y, want.half().float(), rtol=4e-3, atol=4e-3), \
+        (y - want).abs().max().item()
+    assert Kn.device_error() == 0
+
+
+def test_gemm_prefill_shape_remainder_launch_rows():
+    """2048 x 4096 x 14336 (the prefill workload): 444 tiles in the first
+    launch, the last 4 in a K-sliced second one; the rows of the last tile row
+    (both launches) and a band of the first against the oracle."""
+    M, K, N = 2048, 4096, 14336
+    x, packed, scales = _case(M, K, N, seed=11)
+    y = Kn.w4_gemm(x.cuda(), packed, scales).float().cpu()
+    for rows in (slice(1792, 2048), slice(0, 64)):
+        want = _want(x[rows], packed, scales)
+        assert torch.allclose(y[rows], want.half().float(), rtol=4e-3, atol=4e-3), \
+            (y[rows] - want).abs().max().item()
+    assert Kn.device_error() == 0
