@@ -368,7 +368,10 @@ def run_gemv_workload(args, rank, world, local, workload=None, shard=None, cpu=T
           for (M, K, N, dt), n in zip(cases, n_loc)]
     gathered = [torch.empty((world * M, n), dtype=torch.float16, device=device)
                 for (M, K, N, dt), n in zip(cases, n_loc)] if sharded else None
-    cfgs = [Kn.tuned_config(M, K, n, tdt[dt], torch.float16, None, None, device)
+    # the fused peer gather stores from the epilogue of one column tile per CTA
+    one_tile = sharded and args.gather == "peer"
+    cfgs = [Kn.tuned_config(M, K, n, tdt[dt], torch.float16, None, None, device,
+                            streaming=not one_tile)
             for (M, K, N, dt), n in zip(cases, n_loc)]
     n_launch = len(cases)
     stream = torch.cuda.Stream(device)

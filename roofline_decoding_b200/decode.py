@@ -281,7 +281,8 @@ class W4DecodeModel:
                       "gu": (cfg.hidden, 2 * cfg.intermediate), "down": (cfg.intermediate, cfg.hidden)}
             out = {}
             for name, (K, N) in shapes.items():
-                c = tuned_config(1, K, N, bf, bf, None, None, self.device)
+                c = tuned_config(1, K, N, bf, bf, None, None, self.device,
+                                 streaming=self.mode != "fused")
                 if self.mode == "fused" and (K, N) in self.STEP_TILES:
                     c = GemvConfig(*self.STEP_TILES[(K, N)])
                 if name == "gu" and self.gu_block:

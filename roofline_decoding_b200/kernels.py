@@ -198,14 +198,25 @@ def gemv_launch(x2: torch.Tensor, packed: torch.Tensor, scales: torch.Tensor, y:
 
 def tuned_config(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dtype,
                  split_k: int | None, num_warps: int | None,
-                 device: torch.device | None = None, tune: bool = True) -> GemvConfig:
-    """Returns the cached tile for this problem, tuning it first if allowed."""
+                 device: torch.device | None = None, tune: bool = True,
+                 streaming: bool = True) -> GemvConfig:
+    """Returns the cached tile for this problem, tuning it first if allowed.
+
+    streaming=False asks for a tile with one column tile per CTA, which an
+    epilogue (bias, residual, SwiGLU) or the gathered peer output needs; it
+    is tuned and cached separately when the best tile streams.
+    """
     device = device or torch.device("cuda", torch.cuda.current_device())
     _load_tuned_file()
     key = _tune_key(device, M, K, N, x_dtype, y_dtype, split_k, num_warps)
     hit = _TUNE_CACHE.get(key)
-    if hit is not None:
+    if hit is not None and (streaming or len(hit) < 6 or not hit[5]):
         return GemvConfig.from_tuple(hit)
+    if not streaming:
+        key = key + ("one_tile",)
+        hit = _TUNE_CACHE.get(key)
+        if hit is not None:
+            return GemvConfig.from_tuple(hit)
     if not tune or torch.cuda.is_current_stream_capturing():
         return default_config(M, K, N, split_k or 0, num_warps or 0)
     from .tuner import tune_gemv  # local import: the tuner pulls in timing helpers
@@ -213,7 +224,8 @@ def tuned_config(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dt
     with _TUNE_LOCK:
         hit = _TUNE_CACHE.get(key)
         if hit is None:
-            best = tune_gemv(M, K, N, x_dtype, y_dtype, split_k, num_warps, device)
+            best = tune_gemv(M, K, N, x_dtype, y_dtype, split_k, num_warps, device,
+                             streaming=streaming)
             _TUNE_CACHE[key] = best.as_tuple()
             hit = _TUNE_CACHE[key]
     return GemvConfig.from_tuple(hit)

@@ -128,7 +128,8 @@ class PeerGroup:
         x2, squeeze = _prep_x(x, packed.shape[0] * 8, packed.device)
         M, K, N = x2.shape[0], packed.shape[0] * 8, packed.shape[1]
         _, local = self.output(name, M, n_full, out_dtype)
-        cfg = config or tuned_config(M, K, N, x2.dtype, out_dtype, None, None, packed.device)
+        cfg = config or tuned_config(M, K, N, x2.dtype, out_dtype, None, None, packed.device,
+                                     streaming=False)
         po = self.peer_out(name, n_full, col_off)
         stream = torch.cuda.current_stream(packed.device).cuda_stream
         _lib.check(self.lib.w4_gemv_allgather(
