@@ -78,11 +78,22 @@ std::vector<w4_gemv_config> candidates(int M, int K, int N, int split_k, int num
       for (int split : splits) {
         // one CTA per column tile (0), and for large N grids of one or two
         // CTAs per SM in all, each CTA column streaming two or more tiles
-        int col_opts[3] = {0, 0, 0};
+        // ... and the column counts that give every CTA column the same
+        // number of tiles (2..8) with 0.6 to 2 CTAs per SM
+        int col_opts[11] = {0};
         int n_col = 1;
+        auto add_col = [&](int c) {
+          for (int i = 0; i < n_col; ++i)
+            if (col_opts[i] == c) return;
+          col_opts[n_col++] = c;
+        };
         for (int per_sm = 1; per_sm <= 2; ++per_sm) {
           const int c = std::max(1, (per_sm * sms + split / 2) / split);
-          if (2 * c <= tiles && c != col_opts[n_col - 1]) col_opts[n_col++] = c;
+          if (2 * c <= tiles) add_col(c);
+        }
+        for (int t = 2; t <= 8; ++t) {
+          const int c = tiles / t;
+          if (tiles % t == 0 && 10 * c * split >= 6 * sms && c * split <= 2 * sms) add_col(c);
         }
         for (int ci = 0; ci < n_col; ++ci) {
           const int columns = col_opts[ci];
