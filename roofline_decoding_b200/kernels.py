@@ -218,7 +218,10 @@ def tuned_config(M: int, K: int, N: int, x_dtype: torch.dtype, y_dtype: torch.dt
         if hit is not None:
             return GemvConfig.from_tuple(hit)
     if not tune or torch.cuda.is_current_stream_capturing():
-        return default_config(M, K, N, split_k or 0, num_warps or 0)
+        d = default_config(M, K, N, split_k or 0, num_warps or 0)
+        if not streaming and d.columns:  # the default streams for very large N
+            d = GemvConfig(4, 2, 3, 1, 0)
+        return d
     from .tuner import tune_gemv  # local import: the tuner pulls in timing helpers
 
     with _TUNE_LOCK:

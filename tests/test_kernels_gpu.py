@@ -284,6 +284,16 @@ def test_gemv_sixteen_warp_streaming_tiles(strips, row_groups, stages, split, co
         check_gemv(2048, 4104, M=M, bf16=bf16, config=GemvConfig(strips, row_groups, stages, 1, 0))
 
 
+def test_default_tile_streams_for_very_large_n():
+    """Without a tuned entry the library's own tile for a vocab-sized N is the
+    streaming grid of one 16-warp CTA per SM; it matches the oracle."""
+    cfg = K.default_config(1, 1024, 128256)
+    assert cfg.columns > 0 and (cfg.strips, cfg.row_groups) == (4, 4)
+    check_gemv(1024, 128256, bf16=True, config=cfg, seed=5)
+    small = K.default_config(1, 1536, 8960)  # decode-sized N keeps one tile per CTA
+    assert small.columns == 0
+
+
 def test_several_tiles_per_cta_column_needs_a_plain_output():
     """An epilogue reads operands per tile: with fewer CTA columns than tiles
     the launch is refused, not run."""
