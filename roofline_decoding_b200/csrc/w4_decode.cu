@@ -523,8 +523,10 @@ int launch_decode_attention(const void* qkv, const void* cos_t, const void* sin_
 
 // One persistent CTA per SM streams a contiguous range of embedding rows
 // (the tied lm_head) through a ring of shared-memory stages filled by 1-D
-// bulk copies; 8 consumer warps turn each stage's rows into logits.
-constexpr int kLmConsumerWarps = 8;
+// bulk copies; 16 consumer warps turn each stage's rows into logits (one row
+// each per 16-row stage: 73.6 us per 467 MB chained, against 75.9 with 8
+// warps taking two rows each).
+constexpr int kLmConsumerWarps = 16;
 constexpr int kLmThreads = (kLmConsumerWarps + 1) * 32;
 constexpr int kLmRowsPerStage = 16;
 // ring depth: 4 stages of 16 rows (192 KB at hidden 1536), 3 for hidden 2048
