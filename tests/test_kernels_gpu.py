@@ -449,7 +449,8 @@ def test_fused_rmsnorm_prologue_and_bias(M):
     nw = _bf16_dev(1.0 + 0.05 * rng.standard_normal(Kd))
     b = _bf16_dev(0.1 * rng.standard_normal(N))
     y = torch.empty((M, N), dtype=torch.bfloat16, device=DEV)
-    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None)
+    # an epilogue needs one column tile per CTA
+    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None, streaming=False)
     K.fused_launch(x, p, s, y, cfg, _lib.W4_PRO_RMSNORM, nw, 1e-6, _lib.W4_EPI_BIAS, b)
     xf = x.float()
     xn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
@@ -469,7 +470,8 @@ def test_fused_swiglu_prologue_and_residual(M):
     gu = _bf16_dev(rng.standard_normal((M, 2 * Kd)))
     res = _bf16_dev(rng.standard_normal((M, N)))
     y = res.clone()  # in place: residual aliases the output
-    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None)
+    # an epilogue needs one column tile per CTA
+    cfg = K.tuned_config(M, Kd, N, torch.bfloat16, torch.bfloat16, None, None, streaming=False)
     K.fused_launch(gu, p, s, y, cfg, _lib.W4_PRO_SWIGLU, epilogue=_lib.W4_EPI_RESIDUAL, epi_src=y)
     g, u = gu[:, :Kd], gu[:, Kd:]
     act = (torch.nn.functional.silu(g) * u).double()  # bf16 silu, bf16 product

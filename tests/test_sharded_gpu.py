@@ -42,7 +42,9 @@ def _worker(rank, world, port, K, N, M, results):
         peers = PeerGroup(device=dev)
         n_loc = N // world
         mine = shard_columns(packed, scales, rank, world, dev)
-        cfg = Kn.tuned_config(M, K, n_loc, torch.float16, torch.float16, None, None, dev)
+        # the fused gather stores from the epilogue of one column tile per CTA
+        cfg = Kn.tuned_config(M, K, n_loc, torch.float16, torch.float16, None, None, dev,
+                              streaming=False)
         ok = True
         for step in range(5):
             x = torch.randn((M, K), generator=torch.Generator().manual_seed(step)).half().to(dev)
