@@ -42,7 +42,13 @@ def _worker(rank, world, port, K, N, M, results):
         peers = PeerGroup(device=dev)
         n_loc = N // world
         mine = shard_columns(packed, scales, rank, world, dev)
-        # the fused gather stores from the epilogue of one column tile per CTA
+        # Every rank and both gathers must use one tile for the slices to compare
+        # bit for bit, and a tuning run in each process could pick different
+        # ones: fix the shard shape's tile (one column tile per CTA, which the
+        # fused gather needs) before the first call.
+        Kn._load_tuned_file()
+        Kn._TUNE_CACHE[Kn._tune_key(dev, M, K, n_loc, torch.float16, torch.float16, None,
+                                    None)] = (1, 8, 2, 1, 0)
         cfg = Kn.tuned_config(M, K, n_loc, torch.float16, torch.float16, None, None, dev,
                               streaming=False)
         ok = True
