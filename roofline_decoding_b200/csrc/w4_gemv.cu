@@ -18,9 +18,11 @@ void* gemv_kernel_plain(int bf16, int mb, int sw, int rg) {
 namespace {
 
 // The instance a launch uses: plain (one or several tiles per CTA column),
-// the fused decode combination it matches (bf16 activations, up to 8 batch
-// rows), or the generic one.
+// plain with the gathered output, the fused decode combination it matches
+// (bf16 activations, up to 8 batch rows), or the generic one.
 void* pick_kernel(int bf16, int mb, int sw, int rg, int ops, bool tiles) {
+  if (ops == kOpsPeer && !tiles) return gemv_kernel_peer(bf16, mb, sw, rg);
+  if (ops == kOpsPeer) return gemv_kernel_generic(bf16, mb, sw, rg);
   if (ops == kOpsPlain)
     return tiles ? gemv_kernel_plain_tiles(bf16, mb, sw, rg) : gemv_kernel_plain(bf16, mb, sw, rg);
   if (tiles) return gemv_kernel_generic(bf16, mb, sw, rg);
@@ -194,7 +196,7 @@ int gemv_init_device(const DeviceInfo& di) {
       for (int b = 0; b < 2; ++b)
         for (int mb = 1; mb <= 2; ++mb)
           for (void* k : {gemv_kernel_plain(b, mb, sw, rg), gemv_kernel_generic(b, mb, sw, rg),
-                          gemv_kernel_plain_tiles(b, mb, sw, rg)}) {
+                          gemv_kernel_plain_tiles(b, mb, sw, rg), gemv_kernel_peer(b, mb, sw, rg)}) {
             if (!k) continue;  // the 16-warp tiles exist as plain-tiles instances only
             const int st = gemv_kernel_attributes(k, di);
             if (st != W4_OK) return st;
@@ -254,7 +256,8 @@ static int gemv_prepare(const GemvLaunch& L, GemvPrepared* g) {
                 columns, tiles);
 
   const int mb = L.M > 8 ? 2 : 1;
-  const int ops = L.peer ? kOpsGeneric : ops_for(L.ops.prologue, L.ops.epilogue);
+  const int plain_ops = ops_for(L.ops.prologue, L.ops.epilogue);
+  const int ops = !L.peer ? plain_ops : plain_ops == kOpsPlain ? kOpsPeer : kOpsGeneric;
   g->kfn = pick_kernel(L.x_bf16, mb, c.strips, c.row_groups, ops, columns < tiles);
   if (!g->kfn)
     return fail(W4_ERR_UNSUPPORTED, "tile strips=%d row_groups=%d has no instance with a prologue",

@@ -94,9 +94,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // Operation sets a kernel instance is compiled for. A plain GEMV and each
 // fused combination of the decode step get an instance that contains only
 // their own prologue/epilogue code (a smaller kernel: in a chain of dependent
-// launches its post-wait path is fetched faster); any other combination, and
-// the gathered (peer) output, take the generic instance, which selects at run
-// time.
+// launches its post-wait path is fetched faster), and so does the plain GEMV
+// with the gathered (peer) output; any other combination, and a gathered
+// output with a prologue, epilogue or several tiles per CTA, take the generic
+// instance, which selects at run time.
 enum : int {
   kOpsPlain = 0,           // no prologue, no epilogue, local output
   kOpsGeneric = 1,         // prologue, epilogue and peer output chosen at run time
@@ -106,6 +107,7 @@ enum : int {
   kOpsSwigluResidual = 5,  // SwiGLU prologue, residual epilogue (down)
   kOpsRmsSwiglu = 6,       // RMSNorm prologue, SwiGLU epilogue (gate|up, interleaved)
   kOpsPlainTiles = 7,      // plain, CTA columns streaming several column tiles
+  kOpsPeer = 8,            // plain, output gathered into every rank's buffer
 };
 constexpr int kOpsFusedFirst = kOpsRmsBias, kOpsFusedLast = kOpsRmsSwiglu;
 // Instances whose CTA columns may take several column tiles (the others are
@@ -626,7 +628,7 @@ __global__ void __launch_bounds__(TileShape<SW, RG>::kThreads,
   // the instance's operations: compile-time constants except in the generic one
   const int pro = OPS == kOpsGeneric ? p.pro : ops_pro(OPS);
   const int epi = OPS == kOpsGeneric ? p.epi : ops_epi(OPS);
-  const int world = OPS == kOpsGeneric ? pp.world : 0;
+  const int world = (OPS == kOpsGeneric || OPS == kOpsPeer) ? pp.world : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -925,6 +927,7 @@ inline void* gemv_pick_stream_tile(int sw, int rg) {
 void* gemv_kernel_plain(int bf16, int mb, int sw, int rg);
 void* gemv_kernel_generic(int bf16, int mb, int sw, int rg);
 void* gemv_kernel_plain_tiles(int bf16, int mb, int sw, int rg);
+void* gemv_kernel_peer(int bf16, int mb, int sw, int rg);
 void* gemv_kernel_fused(int ops, int sw, int rg);
 
 }  // namespace w4
